@@ -1,0 +1,204 @@
+/*
+ * qi.h — C ABI of libqi.so, the sm_100a (B200) kernels behind qweninfer_b200.
+ *
+ * The library is the device half of a drop-in replacement for the continuous-batching
+ * decode path of QwenInfer (qweninfer/models/qwen2.py, qweninfer/engine/*.py). The
+ * Python package keeps QwenInfer's API and calls these entry points through ctypes.
+ *
+ * Conventions
+ *   - Every pointer argument except the descriptor structs' host arrays is a DEVICE
+ *     pointer owned by the caller (PyTorch tensors). The library never allocates or
+ *     frees memory; scratch buffers are passed in.
+ *   - `stream` is a cudaStream_t (the caller's current stream). Calls only enqueue work
+ *     and never synchronise the host, so they can be captured in a CUDA graph.
+ *   - Return value: 0 on success, a cudaError_t code from the launch, or a QI_ERR_*
+ *     code for rejected arguments. Argument errors are detected on the host before any
+ *     launch.
+ *   - `err` is a device int the kernels set to QI_ERR_TIMEOUT if a bounded wait gives
+ *     up (they never trap or spin forever); the caller reads it after synchronising.
+ *   - Weights are bf16 in the tiled layout produced by qi_tile_offset's mapping
+ *     (128x64 blocks of 8x8 core matrices); activations are fp32; the KV cache is bf16
+ *     with QwenInfer's packed layout (layers, rows, kv_heads=2, max_len, head_dim=64).
+ *   - Compiled for the Qwen2-0.5B block shape: hidden 896, 14 query heads, 2 KV heads,
+ *     head_dim 64, intermediate 4864. Layer count and vocabulary are arguments.
+ */
+#ifndef QI_H_
+#define QI_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QI_OK 0
+#define QI_ERR_ARG 1001     /* an argument is out of range                          */
+#define QI_ERR_TIMEOUT 1002 /* a device-side bounded wait gave up (set in *err)      */
+#define QI_ERR_DEVICE 1003  /* the current device is not an sm_100 part              */
+
+typedef void* qi_stream_t; /* cudaStream_t */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int qi_version(void);
+
+/* One-time per-device setup (kernel attributes). Replaces nothing in the reference:
+ * the reference calls PyTorch/cuBLAS, which set themselves up. Safe to call again. */
+int qi_init(int device);
+
+/* Element offset of W[n][k] in the tiled layout of an (N, K) matrix, N % 128 == 0,
+ * K % 64 == 0. The host-side repack (Qwen2.fuse) uses this mapping. */
+long long qi_tile_offset(int n, int k, int K);
+
+/* ---------------------------------------------------------------- single ops */
+
+/* Embedding lookup into the fp32 residual stream:
+ *   x[t, :] = float(embed[ids[t], :]),  t < M.
+ * Replaces the column gather of qweninfer/models/qwen2.py:273-279 (`embed_t[:, ids]`,
+ * `.float()`). Also zeroes argmax_slots[0..M) (if non-null) for a following
+ * qi_lm_head_argmax. `embed` is the tiled (vocab, 896) table (the tied lm_head). */
+int qi_embed(const uint16_t* embed, int vocab, const int32_t* ids, int M, float* x,
+             unsigned long long* argmax_slots, int* err, qi_stream_t stream);
+
+/* Input RMSNorm + fused QKV projection + bias + RoPE + KV-cache append:
+ *   xn = rmsnorm(x[t]) * ln_w;  qkv = xn @ Wqkv^T + b;  rotate q, k by pos[t];
+ *   q_out[t] = q (fp32, 14x64);  K/V cache[row[t], :, pos[t], :] = bf16(k), bf16(v).
+ * Replaces qweninfer/models/qwen2.py:44-48 (RMSNorm), 160-171 (QKV + bias, view,
+ * apply_rope 86-99) and qweninfer/engine/kv_cache.py:48-60 (KVCache.update scatter).
+ * ln_w may be NULL: x is then used as given (no normalisation).
+ * w_qkv: tiled (1152, 896) with rows permuted so that RoPE pairs (d, d+32) of each head
+ * are adjacent (row 2j <- dim j, row 2j+1 <- dim j+32); b_qkv permuted the same, fp32.
+ * rope_cos/rope_sin: (max_seq, 64) fp32 tables of build_rope_cache (qwen2.py:53-73).
+ * k_layer/v_layer: this layer's cache base, (cache_rows, 2, max_len, 64) bf16. */
+int qi_qkv_rope_append(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv,
+                       const float* b_qkv, const float* rope_cos, const float* rope_sin,
+                       const int32_t* pos, const int32_t* rows, int M, uint16_t* k_layer,
+                       uint16_t* v_layer, int max_len, float* q_out, int* err, qi_stream_t stream);
+
+/* Standalone RMSNorm of M rows of 896 fp32 values (out may alias x):
+ *   out[t] = x[t] * rsqrt(mean(x[t]^2) + eps) * w.
+ * Replaces RMSNorm.forward, qweninfer/models/qwen2.py:44-48, for direct calls of the
+ * module; the model forward fuses the norm into qi_qkv_rope_append /
+ * qi_gate_up_swiglu / qi_lm_head_argmax instead. */
+int qi_rmsnorm(const float* x, const float* w, float eps, int M, float* out, qi_stream_t stream);
+
+/* Standalone RoPE, in place, on fp32 q (B, q_heads, S, 64) and k (B, k_heads, S, 64)
+ * with positions pos (B*S, int32) and the build_rope_cache tables. Replaces apply_rope /
+ * _rotate_half, qweninfer/models/qwen2.py:76-99, for direct calls; the model forward
+ * fuses RoPE into qi_qkv_rope_append. */
+int qi_rope(float* q, int q_heads, float* k, int k_heads, int B, int S, const int32_t* pos,
+            const float* rope_cos, const float* rope_sin, qi_stream_t stream);
+
+/* Ragged GQA attention over each query's own live length (keys 0..pos[t]):
+ *   out[t, h*64:(h+1)*64] = softmax(q[t,h] . K[row,h/7,0..pos]^T / 8) @ V[...]
+ * Replaces the attention core of qweninfer/models/qwen2.py:184-199 (GQA fold, position
+ * mask j <= p, fp32 softmax, @ V, head merge). Keys are split into chunks of
+ * `split_keys` (multiple of 128); `max_splits` >= ceil((max pos + 1) / split_keys).
+ * part: scratch of M*2*max_splits*7*66 floats; counters: M*2 uint32, zero before the
+ * first call (the kernel leaves them zero again). */
+int qi_attention(const float* q, const uint16_t* k_layer, const uint16_t* v_layer,
+                 const int32_t* pos, const int32_t* rows, int M, int max_len, int split_keys,
+                 int max_splits, float* out, float* part, unsigned int* counters, int* err,
+                 qi_stream_t stream);
+
+/* o_proj + residual add into the fp32 stream:  x[t] += attn[t] @ Wo^T.
+ * Replaces qweninfer/models/qwen2.py:203-204 and the residual add of 237-238.
+ * w_o: tiled (896, 896). */
+int qi_o_proj_residual(const float* attn, const uint16_t* w_o, int M, float* x, int* err,
+                       qi_stream_t stream);
+
+/* Post-attention RMSNorm + fused gate/up projection + SwiGLU:
+ *   xn = rmsnorm(x[t]) * ln_w;  h[t, i] = silu(xn . Wg[i]) * (xn . Wu[i]).
+ * Replaces qweninfer/models/qwen2.py:44-48 and 113-116 (w_gate_up, chunk, silu * up).
+ * w_gate_up: tiled (9728, 896), gate row i at 2i and up row i at 2i+1. ln_w may be
+ * NULL: x is then used as given (MLP.forward on an already-normalised input). */
+int qi_gate_up_swiglu(const float* x, const float* ln_w, float eps, const uint16_t* w_gate_up,
+                      int M, float* h, int* err, qi_stream_t stream);
+
+/* down projection + residual add:  x[t] += h[t] @ Wd^T.
+ * Replaces qweninfer/models/qwen2.py:116 (`@ w_down`) and the residual add of 239.
+ * w_down: tiled (896, 4864). */
+int qi_down_residual(const float* h, const uint16_t* w_down, int M, float* x, int* err,
+                     qi_stream_t stream);
+
+/* Final RMSNorm + tied lm_head + greedy argmax:
+ *   xn = rmsnorm(x[t]) * norm_w;  logits[t] = xn @ E^T;  slot[t] = argmax (packed).
+ * Replaces qweninfer/models/qwen2.py:282-292 (norm, last_only, `@ embed_t`) and the
+ * argmax of qweninfer/engine/engine.py:129,155 / generate.py:36,50 (lowest index wins
+ * ties). x rows are read at stride x_stride floats. logits may be null; if non-null it
+ * receives fp32 (logits_bf16 == 0) or bf16 values at row stride logits_ld elements.
+ * argmax_slots (M uint64, zeroed by qi_embed or the caller) receive
+ * (order_key(value) << 32) | (0xffffffff - index); the index is 0xffffffff - low32. */
+int qi_lm_head_argmax(const float* x, long long x_stride, const float* norm_w, float eps,
+                      const uint16_t* embed, int vocab, int M, void* logits, int logits_bf16,
+                      long long logits_ld, unsigned long long* argmax_slots, int* err,
+                      qi_stream_t stream);
+
+/* Row compaction of the packed KV cache: for each (src, dst, length) triple, copy
+ * positions [0, length) of cache row src to row dst in every layer, K and V.
+ * Replaces qweninfer/engine/kv_cache.py:65-73 (KVCache.move_row) as driven by
+ * qweninfer/engine/engine.py:166-179. `moves` is a HOST array of 3*n_moves ints; the
+ * triples are applied in order. */
+int qi_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_rows, int max_len,
+                 const int32_t* moves, int n_moves, qi_stream_t stream);
+
+/* ------------------------------------------------------------- whole forward */
+
+typedef struct {
+  const float* ln1;         /* (896) fp32                               */
+  const uint16_t* w_qkv;    /* tiled (1152, 896), RoPE-pair row order   */
+  const float* b_qkv;       /* (1152) fp32, same row order              */
+  const uint16_t* w_o;      /* tiled (896, 896)                         */
+  const float* ln2;         /* (896) fp32                               */
+  const uint16_t* w_gate_up;/* tiled (9728, 896), gate/up interleaved   */
+  const uint16_t* w_down;   /* tiled (896, 4864)                        */
+} qi_layer;
+
+typedef struct {
+  int num_layers;
+  int vocab;
+  int max_seq;              /* rows of the RoPE tables                  */
+  float eps;
+  const uint16_t* embed;    /* tiled (vocab, 896): lookup and tied head */
+  const float* norm;        /* (896) fp32 final norm                    */
+  const float* rope_cos;    /* (max_seq, 64) fp32                       */
+  const float* rope_sin;
+  const qi_layer* layers;   /* HOST array of num_layers entries         */
+} qi_model;
+
+typedef struct {
+  uint16_t* k;              /* (layers, cache_rows, 2, max_len, 64) bf16 */
+  uint16_t* v;
+  int cache_rows;
+  int max_len;
+} qi_cache;
+
+typedef struct {
+  float* x;                 /* (max_tokens, 896) residual stream         */
+  float* q;                 /* (max_tokens, 896)                         */
+  float* attn;              /* (max_tokens, 896)                         */
+  float* h;                 /* (max_tokens, 4864)                        */
+  float* attn_part;         /* max_tokens*2*max_splits*7*66              */
+  unsigned int* attn_counters; /* max_tokens*2, zero-initialised         */
+  int max_tokens;
+  int max_splits;
+  int split_keys;
+  int* err;                 /* one device int                            */
+} qi_workspace;
+
+/* Full Qwen2 forward of M tokens (qweninfer/models/qwen2.py:263-292 with a cache):
+ * embed, every block (qi_qkv_rope_append, qi_attention, qi_o_proj_residual,
+ * qi_gate_up_swiglu, qi_down_residual), then qi_lm_head_argmax on the tokens listed in
+ * head_tokens (device int32 indices into 0..M-1; null means all M tokens, in order).
+ * ids/pos/rows: device int32 (M). logits/argmax_slots as in qi_lm_head_argmax, with
+ * n_head rows. Batched decode is M = B tokens at S = 1 (engine.py:140-155); a
+ * B = 1 prefill is M = P tokens of one row (engine.py:115-129, generate.py:33-36). */
+int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace* ws,
+               const int32_t* ids, const int32_t* pos, const int32_t* rows, int M,
+               const int32_t* head_tokens, int n_head, void* logits, int logits_bf16,
+               long long logits_ld, unsigned long long* argmax_slots, qi_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QI_H_ */

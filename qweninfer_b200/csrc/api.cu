@@ -1,0 +1,300 @@
+// extern "C" entry points of libqi.so (declared in include/qi.h).
+//
+// Host-side argument checks and launch planning live here; the kernels are in
+// gemv.cu, attention.cu and misc.cu. Nothing here allocates device memory.
+#include <cstdio>
+
+#include "common.cuh"
+#include "internal.h"
+
+using namespace qi;
+
+namespace {
+
+constexpr int kVersion = 100;                 // 0.1.0
+constexpr size_t kSmemBudget = 200 * 1024;    // per GEMV CTA
+
+inline cudaStream_t as_stream(qi_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+inline int rc(cudaError_t e) { return e == cudaSuccess ? QI_OK : (int)e; }
+
+// Token-chunk size of a GEMV: the smallest of 1, 2, 4, 8 covering M, capped by mt_max.
+inline int pick_mt(int M, int mt_max) {
+  int mt = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8;
+  return mt < mt_max ? mt : mt_max;
+}
+
+// Plan and launch one CUDA-core GEMV over an (n_rows, K) tiled weight: one CTA per
+// SM-sized slice of 8-row groups, all 8 warps on each group, and as many groups resident
+// in the shared-memory ring as the budget allows (the rest stream through it).
+int run_gemv(int epi, GemvParams p, int n_rows, int K, int ctas, int mt_max, cudaStream_t s, bool pdl) {
+  p.K = K;
+  p.kr = K;
+  p.n_groups = n_rows / kGroupRows;
+  p.wpg = 8;
+  if (ctas > p.n_groups) ctas = p.n_groups;
+  const int gmax = (p.n_groups + ctas - 1) / ctas;
+  const int mt = pick_mt(p.M, mt_max);
+  const size_t group_bytes = (size_t)(K / kTileK) * kGroupChunkBytes;
+  const size_t fixed = gemv_smem_bytes(mt, K, 0);
+  if (fixed + group_bytes + 8 > kSmemBudget) return QI_ERR_ARG;
+  int fit = (int)((kSmemBudget - fixed) / (group_bytes + 8));
+  p.slots = gmax < fit ? gmax : fit;
+  return rc(launch_gemv(epi, mt, p, ctas, 1, s, pdl));
+}
+
+GemvParams blank_params(int M, int* err) {
+  GemvParams p = {};
+  p.M = M;
+  p.err = err;
+  p.eps = 1e-6f;
+  return p;
+}
+
+int qkv(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv, const float* b_qkv,
+        const float* cos_t, const float* sin_t, const int32_t* pos, const int32_t* rows, int M,
+        uint16_t* kl, uint16_t* vl, int max_len, float* q_out, int* err, cudaStream_t s, bool pdl) {
+  GemvParams p = blank_params(M, err);
+  p.act = x;
+  p.act_stride = kHidden;
+  p.norm_w = ln_w;
+  p.eps = eps;
+  p.out = q_out;
+  p.out_ld = kHidden;
+  p.bias = b_qkv;
+  p.rope_cos = cos_t;
+  p.rope_sin = sin_t;
+  p.pos = pos;
+  p.rows = rows;
+  p.kc = kl;
+  p.vc = vl;
+  p.max_len = max_len;
+  p.w = w_qkv;
+  return run_gemv(kEpiQkvRope, p, kQkvRows, kHidden, sm_count(), 8, s, pdl);
+}
+
+int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int32_t* pos, const int32_t* rows,
+              int M, int max_len, int split_keys, int max_splits, float* out, float* part, unsigned int* counters,
+              int* err, cudaStream_t s, bool pdl) {
+  AttnParams a = {};
+  a.q = q;
+  a.kc = kl;
+  a.vc = vl;
+  a.pos = pos;
+  a.rows = rows;
+  a.M = M;
+  a.max_len = max_len;
+  a.split_keys = split_keys;
+  a.max_splits = max_splits;
+  a.out = out;
+  a.part = part;
+  a.counters = counters;
+  a.err = err;
+  return rc(launch_attention(a, s, pdl));
+}
+
+int oproj(const float* attn, const uint16_t* w_o, int M, float* x, int* err, cudaStream_t s, bool pdl) {
+  GemvParams p = blank_params(M, err);
+  p.act = attn;
+  p.act_stride = kHidden;
+  p.out = x;
+  p.out_ld = kHidden;
+  p.w = w_o;
+  return run_gemv(kEpiResidual, p, kHidden, kHidden, sm_count(), 8, s, pdl);
+}
+
+int gateup(const float* x, const float* ln_w, float eps, const uint16_t* w_gu, int M, float* h, int* err,
+           cudaStream_t s, bool pdl) {
+  GemvParams p = blank_params(M, err);
+  p.act = x;
+  p.act_stride = kHidden;
+  p.norm_w = ln_w;
+  p.eps = eps;
+  p.out = h;
+  p.out_ld = kInter;
+  p.w = w_gu;
+  return run_gemv(kEpiSwiglu, p, kGateUpRows, kHidden, sm_count(), 8, s, pdl);
+}
+
+int down(const float* h, const uint16_t* w_down, int M, float* x, int* err, cudaStream_t s, bool pdl) {
+  GemvParams p = blank_params(M, err);
+  p.act = h;
+  p.act_stride = kInter;
+  p.out = x;
+  p.out_ld = kHidden;
+  p.w = w_down;
+  return run_gemv(kEpiResidual, p, kHidden, kInter, sm_count(), 4, s, pdl);
+}
+
+int lm_head(const float* x, long long x_stride, const int32_t* x_rows, const float* norm_w, float eps,
+            const uint16_t* embed, int vocab, int M, void* logits, int logits_bf16, long long logits_ld,
+            unsigned long long* slots, int* err, cudaStream_t s, bool pdl) {
+  for (int t0 = 0; t0 < M; t0 += 8) {
+    const int m = M - t0 < 8 ? M - t0 : 8;
+    GemvParams p = blank_params(m, err);
+    if (x_rows) {
+      p.act = x;
+      p.act_rows = x_rows + t0;
+    } else {
+      p.act = x + (long long)t0 * x_stride;
+    }
+    p.act_stride = x_stride;
+    p.norm_w = norm_w;
+    p.eps = eps;
+    p.w = embed;
+    if (logits) {
+      const size_t esz = logits_bf16 ? 2 : 4;
+      p.logits = static_cast<uint8_t*>(logits) + (size_t)t0 * logits_ld * esz;
+    }
+    p.logits_bf16 = logits_bf16;
+    p.logits_ld = logits_ld;
+    p.argmax = slots + t0;
+    const int r = run_gemv(kEpiLogits, p, vocab, kHidden, sm_count(), 8, s, pdl && t0 == 0);
+    if (r != QI_OK) return r;
+  }
+  return QI_OK;
+}
+
+bool bad_ptr(const void* p) { return p == nullptr; }
+
+}  // namespace
+
+extern "C" {
+
+int qi_version(void) { return kVersion; }
+
+int qi_init(int device) {
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return (int)e;
+  int major = 0;
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e != cudaSuccess) return (int)e;
+  if (major != 10) return QI_ERR_DEVICE;
+  (void)sm_count();
+  return QI_OK;
+}
+
+long long qi_tile_offset(int n, int k, int K) { return tiled_offset(n, k, K); }
+
+int qi_embed(const uint16_t* embed, int vocab, const int32_t* ids, int M, float* x,
+             unsigned long long* argmax_slots, int* err, qi_stream_t stream) {
+  (void)err;
+  if (M <= 0 || vocab <= 0 || bad_ptr(embed) || bad_ptr(ids) || bad_ptr(x)) return QI_ERR_ARG;
+  return rc(launch_embed(embed, vocab, ids, M, x, argmax_slots, as_stream(stream), false));
+}
+
+int qi_qkv_rope_append(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv,
+                       const float* b_qkv, const float* rope_cos, const float* rope_sin,
+                       const int32_t* pos, const int32_t* rows, int M, uint16_t* k_layer,
+                       uint16_t* v_layer, int max_len, float* q_out, int* err, qi_stream_t stream) {
+  if (M <= 0 || max_len <= 0 || bad_ptr(x) || bad_ptr(w_qkv) || bad_ptr(b_qkv) ||
+      bad_ptr(rope_cos) || bad_ptr(rope_sin) || bad_ptr(pos) || bad_ptr(rows) || bad_ptr(k_layer) ||
+      bad_ptr(v_layer) || bad_ptr(q_out))
+    return QI_ERR_ARG;
+  return qkv(x, ln_w, eps, w_qkv, b_qkv, rope_cos, rope_sin, pos, rows, M, k_layer, v_layer, max_len, q_out,
+             err, as_stream(stream), false);
+}
+
+int qi_attention(const float* q, const uint16_t* k_layer, const uint16_t* v_layer, const int32_t* pos,
+                 const int32_t* rows, int M, int max_len, int split_keys, int max_splits, float* out,
+                 float* part, unsigned int* counters, int* err, qi_stream_t stream) {
+  if (M <= 0 || max_len <= 0 || split_keys <= 0 || split_keys % 128 != 0 || max_splits <= 0 ||
+      (long long)split_keys * max_splits < max_len || bad_ptr(q) || bad_ptr(k_layer) || bad_ptr(v_layer) ||
+      bad_ptr(pos) || bad_ptr(rows) || bad_ptr(out) || (max_splits > 1 && (bad_ptr(part) || bad_ptr(counters))))
+    return QI_ERR_ARG;
+  return attention(q, k_layer, v_layer, pos, rows, M, max_len, split_keys, max_splits, out, part, counters, err,
+                   as_stream(stream), false);
+}
+
+int qi_o_proj_residual(const float* attn, const uint16_t* w_o, int M, float* x, int* err, qi_stream_t stream) {
+  if (M <= 0 || bad_ptr(attn) || bad_ptr(w_o) || bad_ptr(x)) return QI_ERR_ARG;
+  return oproj(attn, w_o, M, x, err, as_stream(stream), false);
+}
+
+int qi_gate_up_swiglu(const float* x, const float* ln_w, float eps, const uint16_t* w_gate_up, int M, float* h,
+                      int* err, qi_stream_t stream) {
+  if (M <= 0 || bad_ptr(x) || bad_ptr(w_gate_up) || bad_ptr(h)) return QI_ERR_ARG;
+  return gateup(x, ln_w, eps, w_gate_up, M, h, err, as_stream(stream), false);
+}
+
+int qi_down_residual(const float* h, const uint16_t* w_down, int M, float* x, int* err, qi_stream_t stream) {
+  if (M <= 0 || bad_ptr(h) || bad_ptr(w_down) || bad_ptr(x)) return QI_ERR_ARG;
+  return down(h, w_down, M, x, err, as_stream(stream), false);
+}
+
+int qi_lm_head_argmax(const float* x, long long x_stride, const float* norm_w, float eps, const uint16_t* embed,
+                      int vocab, int M, void* logits, int logits_bf16, long long logits_ld,
+                      unsigned long long* argmax_slots, int* err, qi_stream_t stream) {
+  if (M <= 0 || vocab <= 0 || vocab % kTileRows != 0 || x_stride < kHidden || bad_ptr(x) || bad_ptr(norm_w) ||
+      bad_ptr(embed) || bad_ptr(argmax_slots) || (logits && logits_ld < vocab))
+    return QI_ERR_ARG;
+  return lm_head(x, x_stride, nullptr, norm_w, eps, embed, vocab, M, logits, logits_bf16, logits_ld, argmax_slots,
+                 err, as_stream(stream), false);
+}
+
+int qi_rmsnorm(const float* x, const float* w, float eps, int M, float* out, qi_stream_t stream) {
+  if (M <= 0 || bad_ptr(x) || bad_ptr(w) || bad_ptr(out)) return QI_ERR_ARG;
+  return rc(launch_rmsnorm(x, w, eps, M, out, as_stream(stream)));
+}
+
+int qi_rope(float* q, int q_heads, float* k, int k_heads, int B, int S, const int32_t* pos, const float* rope_cos,
+            const float* rope_sin, qi_stream_t stream) {
+  if (B <= 0 || S <= 0 || q_heads < 0 || k_heads < 0 || bad_ptr(pos) || bad_ptr(rope_cos) || bad_ptr(rope_sin) ||
+      (q_heads > 0 && bad_ptr(q)) || (k_heads > 0 && bad_ptr(k)))
+    return QI_ERR_ARG;
+  return rc(launch_rope(q, q_heads, k, k_heads, B, S, pos, rope_cos, rope_sin, as_stream(stream)));
+}
+
+int qi_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_rows, int max_len, const int32_t* moves,
+                 int n_moves, qi_stream_t stream) {
+  if (layers <= 0 || cache_rows <= 0 || max_len <= 0 || n_moves < 0 || bad_ptr(k) || bad_ptr(v) ||
+      (n_moves > 0 && bad_ptr(moves)))
+    return QI_ERR_ARG;
+  for (int i = 0; i < n_moves; ++i) {
+    const int src = moves[3 * i], dst = moves[3 * i + 1], len = moves[3 * i + 2];
+    if (src < 0 || src >= cache_rows || dst < 0 || dst >= cache_rows || len < 0 || len > max_len) return QI_ERR_ARG;
+  }
+  for (int i = 0; i < n_moves; ++i) {
+    const int r = rc(launch_move_rows(k, v, layers, cache_rows, max_len, moves[3 * i], moves[3 * i + 1],
+                                      moves[3 * i + 2], as_stream(stream)));
+    if (r != QI_OK) return r;
+  }
+  return QI_OK;
+}
+
+int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
+               const int32_t* pos, const int32_t* rows, int M, const int32_t* head_tokens, int n_head, void* logits,
+               int logits_bf16, long long logits_ld, unsigned long long* argmax_slots, qi_stream_t stream) {
+  if (!model || !cache || !ws || !model->layers || M <= 0 || M > ws->max_tokens || n_head < 0 ||
+      (head_tokens == nullptr && n_head != 0 && n_head != M) || bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) ||
+      (n_head > 0 && bad_ptr(argmax_slots)) || model->vocab % kTileRows != 0 || model->num_layers <= 0 ||
+      ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len)
+    return QI_ERR_ARG;
+  cudaStream_t s = as_stream(stream);
+  const bool pdl = true;
+  int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, argmax_slots, s, false));
+  if (r != QI_OK) return r;
+  const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
+  for (int li = 0; li < model->num_layers; ++li) {
+    const qi_layer& L = model->layers[li];
+    uint16_t* kl = cache->k + li * layer_elems;
+    uint16_t* vl = cache->v + li * layer_elems;
+    r = qkv(ws->x, L.ln1, model->eps, L.w_qkv, L.b_qkv, model->rope_cos, model->rope_sin, pos, rows, M, kl, vl,
+            cache->max_len, ws->q, ws->err, s, pdl);
+    if (r != QI_OK) return r;
+    r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, ws->attn,
+                  ws->attn_part, ws->attn_counters, ws->err, s, pdl);
+    if (r != QI_OK) return r;
+    r = oproj(ws->attn, L.w_o, M, ws->x, ws->err, s, pdl);
+    if (r != QI_OK) return r;
+    r = gateup(ws->x, L.ln2, model->eps, L.w_gate_up, M, ws->h, ws->err, s, pdl);
+    if (r != QI_OK) return r;
+    r = down(ws->h, L.w_down, M, ws->x, ws->err, s, pdl);
+    if (r != QI_OK) return r;
+  }
+  if (n_head > 0)
+    r = lm_head(ws->x, kHidden, head_tokens, model->norm, model->eps, model->embed, model->vocab, n_head, logits,
+                logits_bf16, logits_ld, argmax_slots, ws->err, s, pdl);
+  return r;
+}
+
+}  // extern "C"

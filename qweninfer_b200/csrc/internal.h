@@ -1,0 +1,86 @@
+// Internal launcher interfaces shared by the .cu files of libqi.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qi {
+
+enum GemvEpilogue : int {
+  kEpiQkvRope = 0,   // bias + RoPE; q -> fp32 buffer, k/v -> bf16 cache
+  kEpiResidual = 1,  // out[t, n] += value
+  kEpiSwiglu = 2,    // h[t, i] = silu(gate) * up (gate/up rows interleaved)
+  kEpiLogits = 3,    // optional logits store + packed argmax
+};
+
+struct GemvParams {
+  const uint16_t* w;       // tiled weights
+  int K;                   // full inner dimension
+  int kr;                  // inner range per split (multiple of 64)
+  int n_groups;            // output rows / 8
+  int wpg;                 // warps per 8-row group (1, 2, 4, 8)
+  int slots;               // weight slots (in groups) of the shared-memory ring
+  int M;                   // tokens
+  const float* act;        // (., K) fp32 input rows
+  long long act_stride;    // floats between consecutive token rows
+  const int32_t* act_rows; // optional token -> input row index (lm_head gather)
+  const float* norm_w;     // RMSNorm weight (fp32) for norm-prologue kernels
+  float eps;
+  // epilogues
+  float* out;
+  int out_ld;
+  const float* bias;
+  const float* rope_cos;
+  const float* rope_sin;
+  const int32_t* pos;
+  const int32_t* rows;
+  uint16_t* kc;
+  uint16_t* vc;
+  int max_len;
+  void* logits;
+  int logits_bf16;
+  long long logits_ld;
+  unsigned long long* argmax;
+  int* err;
+};
+
+// Dynamic shared memory of one GEMV CTA (mt tokens per chunk, kr columns, slots groups).
+size_t gemv_smem_bytes(int mt, int kr, int slots);
+
+// Launch a GEMV of the given epilogue with mt tokens per chunk (1, 2, 4 or 8);
+// splits > 1 only for kEpiResidual. kEpiLogits requires M <= mt.
+cudaError_t launch_gemv(int epi, int mt, GemvParams p, int ctas, int splits, cudaStream_t stream, bool pdl);
+
+struct AttnParams {
+  const float* q;
+  const uint16_t* kc;
+  const uint16_t* vc;
+  const int32_t* pos;
+  const int32_t* rows;
+  int M;
+  int max_len;
+  int split_keys;
+  int max_splits;
+  float* out;
+  float* part;
+  unsigned int* counters;
+  int* err;
+};
+
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
+
+cudaError_t launch_embed(const uint16_t* embed, int vocab, const int32_t* ids, int M, float* x,
+                         unsigned long long* slots, cudaStream_t stream, bool pdl);
+
+cudaError_t launch_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_rows, int max_len,
+                             int src, int dst, int length, cudaStream_t stream);
+
+cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int M, float* out, cudaStream_t s);
+
+cudaError_t launch_rope(float* q, int hq, float* k, int hk, int B, int S, const int32_t* pos, const float* cos_t,
+                        const float* sin_t, cudaStream_t s);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+}  // namespace qi
