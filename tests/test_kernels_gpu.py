@@ -107,9 +107,9 @@ def test_mlp_kernels():
     with torch.no_grad():
         for p in mlp.parameters():
             p.normal_(0, 0.02)
-    wg = bf16_round(mlp.gate_proj.weight.numpy())
-    wu = bf16_round(mlp.up_proj.weight.numpy())
-    wd = bf16_round(mlp.down_proj.weight.numpy())
+    wg = bf16_round(mlp.gate_proj.weight.detach().numpy())
+    wu = bf16_round(mlp.up_proj.weight.detach().numpy())
+    wd = bf16_round(mlp.down_proj.weight.detach().numpy())
     mlp.fuse()
     mlp.to(DEV)
     rng = np.random.default_rng(2)
@@ -171,7 +171,9 @@ def test_qkv_rope_append(M):
     # nothing else was written
     written = np.zeros((rows_total, max_len), bool)
     written[rows, pos] = True
-    assert np.all(kc_h[~written] == 0) and np.all(vc_h[~written] == 0)
+    k_slots = kc_h.transpose(0, 2, 1, 3)   # (rows, max_len, 2, 64)
+    v_slots = vc_h.transpose(0, 2, 1, 3)
+    assert np.all(k_slots[~written] == 0) and np.all(v_slots[~written] == 0)
 
 
 @pytest.mark.parametrize("M,max_len,positions", [
