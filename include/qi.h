@@ -175,27 +175,65 @@ typedef struct {
 typedef struct {
   float* x;                 /* (max_tokens, 896) residual stream         */
   float* q;                 /* (max_tokens, 896)                         */
-  float* attn;              /* (max_tokens, 896)                         */
-  float* h;                 /* (max_tokens, 4864)                        */
+  float* attn;              /* (max_tokens, 896), CUDA-core path         */
+  float* h;                 /* (max_tokens, 4864), CUDA-core path        */
   float* attn_part;         /* max_tokens*2*max_splits*7*66              */
   unsigned int* attn_counters; /* max_tokens*2, zero-initialised         */
   int max_tokens;
   int max_splits;
   int split_keys;
   int* err;                 /* one device int                            */
+  /* tensor-core path (use_tc = 1, the default of the Python package) */
+  int use_tc;
+  uint16_t* act_x;          /* activation tiles, K = 896: ss_ld * 3584 bytes  */
+  uint16_t* act_attn;       /* same size                                      */
+  uint16_t* act_h;          /* K = 4864: ss_ld * 19456 bytes                  */
+  float* ss;                /* 7 * ss_ld floats: per-128-feature sums of squares */
+  int ss_ld;                /* >= tokens rounded up to the token tile          */
+  float* tc_scratch;        /* stream-K partials, >= 148*2*128*token_tile floats */
+  long long tc_scratch_floats;
+  unsigned int* tc_counters;/* one per output tile, zero-initialised          */
+  int tc_counters_len;
 } qi_workspace;
 
 /* Full Qwen2 forward of M tokens (qweninfer/models/qwen2.py:263-292 with a cache):
- * embed, every block (qi_qkv_rope_append, qi_attention, qi_o_proj_residual,
- * qi_gate_up_swiglu, qi_down_residual), then qi_lm_head_argmax on the tokens listed in
- * head_tokens (device int32 indices into 0..M-1; null means all M tokens, in order).
- * ids/pos/rows: device int32 (M). logits/argmax_slots as in qi_lm_head_argmax, with
- * n_head rows. Batched decode is M = B tokens at S = 1 (engine.py:140-155); a
- * B = 1 prefill is M = P tokens of one row (engine.py:115-129, generate.py:33-36). */
+ * embedding, every block (RMSNorm + QKV + bias + RoPE + KV append, ragged attention,
+ * o_proj + residual, RMSNorm + gate/up + SwiGLU, down + residual), final RMSNorm, tied
+ * head and greedy argmax of the head tokens t = head_lo + i*head_stride, i < n_head
+ * (n_head = 0: no head). ids/pos/rows: device int32 (M). logits (optional, row i for head
+ * token i) and argmax_slots (n_head) as in qi_lm_head_argmax. Batched decode is M = B
+ * tokens at S = 1 (engine.py:140-155); a B = 1 prefill is M = P tokens of one row with
+ * head_lo = P-1 (engine.py:115-129, generate.py:33-36).
+ * ws->use_tc selects the tcgen05 projections (activation tiles, stream-K) or the
+ * CUDA-core GEMV kernels of the single-op entry points above. */
 int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace* ws,
-               const int32_t* ids, const int32_t* pos, const int32_t* rows, int M,
-               const int32_t* head_tokens, int n_head, void* logits, int logits_bf16,
-               long long logits_ld, unsigned long long* argmax_slots, qi_stream_t stream);
+               const int32_t* ids, const int32_t* pos, const int32_t* rows, int M, int head_lo,
+               int head_stride, int n_head, void* logits, int logits_bf16, long long logits_ld,
+               unsigned long long* argmax_slots, qi_stream_t stream);
+
+/* ------------------------------------------------- tensor-core building blocks */
+
+/* fp32 activations x (M, K) -> activation tiles of norm_w * x (norm_w may be NULL) for
+ * token tile NT (8..128, power of two): [t/NT][k/64][hi|lo][(t%NT)/8][(k%64)/8][t%8][k%8]
+ * bf16, hi = bf16(v), lo = bf16(v - hi). With ss non-NULL (K = 896 only): ss[0][t] =
+ * sum_k x[t,k]^2 and ss[1..6][t] = 0, row stride ss_ld. Tokens M..(M rounded up to NT)-1
+ * are written as zeros. No reference counterpart: this is the operand format of
+ * qi_tc_linear and of the forward's tensor-core projections. */
+int qi_act_tiles(const float* x, const float* norm_w, int M, int K, int NT, uint16_t* act,
+                 float* ss, int ss_ld, qi_stream_t stream);
+
+/* One tensor-core projection (tcgen05 UMMA, TMEM accumulators, stream-K over `ctas`
+ * CTAs; 0 = one per SM):  out[t, n] = r[t] * sum_k W[n, k] * x[t, k]  for the
+ * activations encoded in `act` (qi_act_tiles), with r[t] = rsqrt(sum_j ss[j][t] / 896 +
+ * eps) when ss is non-NULL (RMSNorm folded as in the forward) and 1 otherwise.
+ * W: tiled (n_rows, K), n_rows % 128 == 0, K % 64 == 0. scratch: scratch_floats floats
+ * (>= 2*128*NT per CTA); counters: counters_len uint32 >= (n_rows/128)*ceil(M/NT),
+ * zero before the call and left zero. The x @ W^T of every projection in
+ * qweninfer/models/qwen2.py (160-162, 203-204, 114-116, 291). */
+int qi_tc_linear(const uint16_t* w, int n_rows, int K, const uint16_t* act, int M, int NT,
+                 const float* ss, int ss_ld, float eps, float* out, int out_ld, float* scratch,
+                 long long scratch_floats, unsigned int* counters, int counters_len, int ctas,
+                 int* err, qi_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -44,7 +44,9 @@ class QiCache(C.Structure):
 class QiWorkspace(C.Structure):
     _fields_ = [("x", vp), ("q", vp), ("attn", vp), ("h", vp), ("attn_part", vp),
                 ("attn_counters", vp), ("max_tokens", i32), ("max_splits", i32),
-                ("split_keys", i32), ("err", vp)]
+                ("split_keys", i32), ("err", vp), ("use_tc", i32), ("act_x", vp), ("act_attn", vp),
+                ("act_h", vp), ("ss", vp), ("ss_ld", i32), ("tc_scratch", vp), ("tc_scratch_floats", i64),
+                ("tc_counters", vp), ("tc_counters_len", i32)]
 
 
 # name -> (restype, argtypes), exactly the declarations of include/qi.h
@@ -63,7 +65,9 @@ SIGNATURES = {
     "qi_rope": (i32, [vp, i32, vp, i32, i32, i32, vp, vp, vp, vp]),
     "qi_move_rows": (i32, [vp, vp, i32, i32, i32, C.POINTER(i32), i32, vp]),
     "qi_forward": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp,
-                         i32, vp, i32, vp, i32, i64, vp, vp]),
+                         i32, i32, i32, i32, vp, i32, i64, vp, vp]),
+    "qi_act_tiles": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp]),
+    "qi_tc_linear": (i32, [vp, i32, i32, vp, i32, i32, vp, i32, f32, vp, i32, vp, i64, vp, i32, i32, vp, vp]),
 }
 
 _lock = threading.Lock()

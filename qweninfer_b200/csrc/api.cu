@@ -6,6 +6,7 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "tc_proj.h"
 
 using namespace qi;
 
@@ -74,8 +75,10 @@ int qkv(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv, con
 
 int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int32_t* pos, const int32_t* rows,
               int M, int max_len, int split_keys, int max_splits, float* out, float* part, unsigned int* counters,
-              int* err, cudaStream_t s, bool pdl) {
+              int* err, cudaStream_t s, bool pdl, uint16_t* out_act = nullptr, int out_nt = 0) {
   AttnParams a = {};
+  a.out_act = out_act;
+  a.out_nt = out_nt;
   a.q = q;
   a.kc = kl;
   a.vc = vl;
@@ -155,6 +158,146 @@ int lm_head(const float* x, long long x_stride, const int32_t* x_rows, const flo
 }
 
 bool bad_ptr(const void* p) { return p == nullptr; }
+
+inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
+inline bool bad_nt(int NT) { return NT < 8 || NT > 128 || (NT & (NT - 1)) != 0; }
+
+// Token tile of a forward over M tokens: the power of two >= M (at least 8), at most 128.
+inline int token_tile(int M) {
+  int nt = 8;
+  while (nt < M && nt < 128) nt <<= 1;
+  return nt;
+}
+
+// Plan and launch one tensor-core projection: grid = min(SMs, units, scratch capacity),
+// pipeline stages within a ~100 KB shared-memory budget, TMEM for two accumulators.
+int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* counters, int counters_len,
+           int ctas, cudaStream_t s, bool pdl) {
+  const long long units = (long long)p.n_mtiles * p.n_ntiles * p.KB;
+  if ((long long)p.n_mtiles * p.n_ntiles > counters_len) return QI_ERR_ARG;
+  int g = ctas > 0 ? ctas : sm_count();
+  if (g > units) g = (int)units;
+  const long long per_cta = 2LL * 128 * p.NT;
+  if (scratch_floats / per_cta < g) g = (int)(scratch_floats / per_cta);
+  if (g < 1) return QI_ERR_ARG;
+  const size_t stage = 16384 + (size_t)p.NT * 256;
+  int stages = (int)((100 * 1024) / stage);
+  stages = stages < 2 ? 2 : (stages > 8 ? 8 : stages);
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(4 * p.NT)) cols <<= 1;
+  p.scratch = scratch;
+  p.counters = counters;
+  p.stages = stages;
+  p.tmem_cols = cols;
+  return rc(launch_tc_proj(p, g, s, pdl));
+}
+
+// qi_forward on the tensor-core path: every projection is a tc_proj launch whose
+// epilogue writes the next projection's activation tiles (the RMSNorm weights folded in,
+// the per-token RMS applied in the consumer's epilogue from partial sums of squares).
+int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
+               const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
+               void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots, cudaStream_t s) {
+  const int NT = token_tile(M);
+  const int n_nt = (M + NT - 1) / NT;
+  if (n_nt * NT > ws->ss_ld || !ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss || !ws->tc_scratch ||
+      !ws->tc_counters)
+    return QI_ERR_ARG;
+  const bool pdl = true;
+  int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, slots, s, false, model->layers[0].ln1, NT,
+                          ws->act_x, ws->ss, ws->ss_ld));
+  if (r != QI_OK) return r;
+  TcParams base = {};
+  base.NT = NT;
+  base.n_ntiles = n_nt;
+  base.M = M;
+  base.ss_ld = ws->ss_ld;
+  base.eps = model->eps;
+  base.err = ws->err;
+  auto launch = [&](TcParams& p) {
+    return run_tc(p, ws->tc_scratch, ws->tc_scratch_floats, ws->tc_counters, ws->tc_counters_len, 0, s, pdl);
+  };
+  const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
+  for (int li = 0; li < model->num_layers; ++li) {
+    const qi_layer& L = model->layers[li];
+    uint16_t* kl = cache->k + li * layer_elems;
+    uint16_t* vl = cache->v + li * layer_elems;
+    TcParams p = base;  // RMSNorm + QKV + bias + RoPE + KV append
+    p.w = L.w_qkv;
+    p.KB = kHidden / 64;
+    p.n_mtiles = kQkvRows / 128;
+    p.act_in = ws->act_x;
+    p.ss_in = ws->ss;
+    p.epi = kTcQkvRope;
+    p.bias = L.b_qkv;
+    p.rope_cos = model->rope_cos;
+    p.rope_sin = model->rope_sin;
+    p.pos = pos;
+    p.rows = rows;
+    p.q = ws->q;
+    p.kc = kl;
+    p.vc = vl;
+    p.max_len = cache->max_len;
+    if ((r = launch(p)) != QI_OK) return r;
+    r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
+                  ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, NT);
+    if (r != QI_OK) return r;
+    p = base;  // o_proj + residual; emits RMSNorm(post_attention) inputs
+    p.w = L.w_o;
+    p.KB = kHidden / 64;
+    p.n_mtiles = kHidden / 128;
+    p.act_in = ws->act_attn;
+    p.epi = kTcResidual;
+    p.x = ws->x;
+    p.next_norm_w = L.ln2;
+    p.act_out = ws->act_x;
+    p.ss_out = ws->ss;
+    if ((r = launch(p)) != QI_OK) return r;
+    p = base;  // gate/up + SwiGLU
+    p.w = L.w_gate_up;
+    p.KB = kHidden / 64;
+    p.n_mtiles = kGateUpRows / 128;
+    p.act_in = ws->act_x;
+    p.ss_in = ws->ss;
+    p.epi = kTcSwiglu;
+    p.act_out = ws->act_h;
+    if ((r = launch(p)) != QI_OK) return r;
+    p = base;  // down + residual; emits the next norm's inputs
+    p.w = L.w_down;
+    p.KB = kInter / 64;
+    p.n_mtiles = kHidden / 128;
+    p.act_in = ws->act_h;
+    p.epi = kTcResidual;
+    p.x = ws->x;
+    p.next_norm_w = li + 1 < model->num_layers ? model->layers[li + 1].ln1 : model->norm;
+    p.act_out = ws->act_x;
+    p.ss_out = ws->ss;
+    if ((r = launch(p)) != QI_OK) return r;
+  }
+  if (n_head > 0) {
+    const int head_hi = head_lo + (n_head - 1) * head_stride + 1;
+    for (int nt = head_lo / NT; nt <= (head_hi - 1) / NT; ++nt) {
+      TcParams p = base;  // final RMSNorm + tied head + argmax, one token tile per launch
+      p.w = model->embed;
+      p.KB = kHidden / 64;
+      p.n_mtiles = model->vocab / 128;
+      p.act_in = ws->act_x;
+      p.ss_in = ws->ss;
+      p.n_ntiles = 1;
+      p.ntile0 = nt;
+      p.epi = kTcLogits;
+      p.logits = logits;
+      p.logits_bf16 = logits_bf16;
+      p.logits_ld = logits_ld;
+      p.argmax = slots;
+      p.head_lo = head_lo;
+      p.head_hi = head_hi;
+      p.head_stride = head_stride;
+      if ((r = launch(p)) != QI_OK) return r;
+    }
+  }
+  return QI_OK;
+}
 
 }  // namespace
 
@@ -261,14 +404,51 @@ int qi_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_rows, int max_l
   return QI_OK;
 }
 
+int qi_act_tiles(const float* x, const float* norm_w, int M, int K, int NT, uint16_t* act, float* ss, int ss_ld,
+                 qi_stream_t stream) {
+  if (M <= 0 || K <= 0 || K % 64 != 0 || bad_nt(NT) || bad_ptr(x) || bad_ptr(act) ||
+      (ss && (K != kHidden || ss_ld < round_up(M, NT))))
+    return QI_ERR_ARG;
+  return rc(launch_act_tiles(x, norm_w, M, K, NT, act, ss, ss_ld, as_stream(stream), false));
+}
+
+int qi_tc_linear(const uint16_t* w, int n_rows, int K, const uint16_t* act, int M, int NT, const float* ss, int ss_ld,
+                 float eps, float* out, int out_ld, float* scratch, long long scratch_floats, unsigned int* counters,
+                 int counters_len, int ctas, int* err, qi_stream_t stream) {
+  if (M <= 0 || n_rows <= 0 || n_rows % 128 != 0 || K <= 0 || K % 64 != 0 || bad_nt(NT) || bad_ptr(w) ||
+      bad_ptr(act) || bad_ptr(out) || out_ld < n_rows || bad_ptr(scratch) || bad_ptr(counters) ||
+      (ss && (K != kHidden || ss_ld < round_up(M, NT))))
+    return QI_ERR_ARG;
+  TcParams p = {};
+  p.w = w;
+  p.KB = K / 64;
+  p.n_mtiles = n_rows / 128;
+  p.act_in = act;
+  p.NT = NT;
+  p.n_ntiles = (M + NT - 1) / NT;
+  p.M = M;
+  p.ss_in = ss;
+  p.ss_ld = ss_ld;
+  p.eps = eps;
+  p.epi = kTcPlain;
+  p.out = out;
+  p.out_ld = out_ld;
+  p.err = err;
+  return run_tc(p, scratch, scratch_floats, counters, counters_len, ctas, as_stream(stream), false);
+}
+
 int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
-               const int32_t* pos, const int32_t* rows, int M, const int32_t* head_tokens, int n_head, void* logits,
-               int logits_bf16, long long logits_ld, unsigned long long* argmax_slots, qi_stream_t stream) {
+               const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
+               void* logits, int logits_bf16, long long logits_ld, unsigned long long* argmax_slots,
+               qi_stream_t stream) {
   if (!model || !cache || !ws || !model->layers || M <= 0 || M > ws->max_tokens || n_head < 0 ||
-      (head_tokens == nullptr && n_head != 0 && n_head != M) || bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) ||
-      (n_head > 0 && bad_ptr(argmax_slots)) || model->vocab % kTileRows != 0 || model->num_layers <= 0 ||
+      (n_head > 0 && (head_lo < 0 || head_stride < 1 || (long long)head_lo + (long long)(n_head - 1) * head_stride >= M)) ||
+      bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || (n_head > 0 && bad_ptr(argmax_slots)) ||
+      (logits && logits_ld < model->vocab) || model->vocab % kTileRows != 0 || model->num_layers <= 0 ||
       ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len)
     return QI_ERR_ARG;
+  if (ws->use_tc) return forward_tc(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits,
+                                    logits_bf16, logits_ld, argmax_slots, as_stream(stream));
   cudaStream_t s = as_stream(stream);
   const bool pdl = true;
   int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, argmax_slots, s, false));
@@ -292,8 +472,9 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
     if (r != QI_OK) return r;
   }
   if (n_head > 0)
-    r = lm_head(ws->x, kHidden, head_tokens, model->norm, model->eps, model->embed, model->vocab, n_head, logits,
-                logits_bf16, logits_ld, argmax_slots, ws->err, s, pdl);
+    r = lm_head(ws->x + (long long)head_lo * kHidden, (long long)head_stride * kHidden, nullptr, model->norm,
+                model->eps, model->embed, model->vocab, n_head, logits, logits_bf16, logits_ld, argmax_slots,
+                ws->err, s, pdl);
   return r;
 }
 

@@ -11,6 +11,7 @@
 // the splits in split order and resets its counter.
 #include "common.cuh"
 #include "internal.h"
+#include "tc_proj.h"
 
 namespace qi {
 
@@ -29,6 +30,17 @@ struct AttnSmem {
   uint64_t bar[2];
   int last;
 };
+
+// Output element (token, feature f = head * 64 + d): fp32 and/or the o projection's
+// activation tiles (hi/lo bf16 halves).
+__device__ __forceinline__ void emit(const AttnParams& p, int tok, int f, float v) {
+  if (p.out) p.out[(long long)tok * kHidden + f] = v;
+  if (p.out_act) {
+    const uint16_t hi = f32_to_bf16_rn(v);
+    p.out_act[act_offset(tok, f, 0, kHidden, p.out_nt)] = hi;
+    p.out_act[act_offset(tok, f, 1, kHidden, p.out_nt)] = f32_to_bf16_rn(v - bf16_to_f32(hi));
+  }
+}
 
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -188,7 +200,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
       if (d < kHeadDim) A = fmaf(sc, S.cmb[w][h][d], A);
     }
     if (nsplit == 1) {
-      if (d < kHeadDim) p.out[(long long)tok * kHidden + (g * kGqa + h) * kHeadDim + d] = A / L;
+      if (d < kHeadDim) emit(p, tok, (g * kGqa + h) * kHeadDim + d, A / L);
     } else {
       part[idx] = d < kHeadDim ? A : (d == kHeadDim ? mx : L);
     }
@@ -217,7 +229,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
       L = fmaf(sc, __ldcg(ph + kHeadDim + 1), L);
       A = fmaf(sc, __ldcg(ph + d), A);
     }
-    p.out[(long long)tok * kHidden + (g * kGqa + h) * kHeadDim + d] = A / L;
+    emit(p, tok, (g * kGqa + h) * kHeadDim + d, A / L);
   }
   if (tid == 0) p.counters[tok * kKvHeads + g] = 0u;
 }

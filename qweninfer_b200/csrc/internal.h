@@ -61,7 +61,9 @@ struct AttnParams {
   int max_len;
   int split_keys;
   int max_splits;
-  float* out;
+  float* out;         // fp32 (M, 896), may be null
+  uint16_t* out_act;  // activation tiles (K = 896, token tile out_nt) for the o projection, may be null
+  int out_nt;
   float* part;
   unsigned int* counters;
   int* err;
@@ -69,8 +71,11 @@ struct AttnParams {
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 
+// norm_w/NT/act/ss (optional, all or none): also emit activation tiles of norm_w * x and
+// per-token sums of squares for the tensor-core projections (tc_proj.h).
 cudaError_t launch_embed(const uint16_t* embed, int vocab, const int32_t* ids, int M, float* x,
-                         unsigned long long* slots, cudaStream_t stream, bool pdl);
+                         unsigned long long* slots, cudaStream_t stream, bool pdl, const float* norm_w = nullptr,
+                         int NT = 0, uint16_t* act = nullptr, float* ss = nullptr, int ss_ld = 0);
 
 cudaError_t launch_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_rows, int max_len,
                              int src, int dst, int length, cudaStream_t stream);

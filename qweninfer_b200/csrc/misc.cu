@@ -1,6 +1,7 @@
 // Small kernels: embedding gather into the fp32 residual stream and KV row compaction.
 #include "common.cuh"
 #include "internal.h"
+#include "tc_proj.h"
 
 namespace qi {
 
@@ -8,23 +9,54 @@ namespace {
 
 // One CTA per token; 112 threads each move one 8-element core-matrix row of the tiled
 // (vocab, 896) table (qweninfer/models/qwen2.py:273-279: embed lookup, .float()).
+// With `act` set it also writes the first projection's activation tiles of
+// norm_w * x and the token's sum of squares into ss[0][t] (ss[1..6][t] = 0).
 __global__ void __launch_bounds__(128) embed_kernel(const uint16_t* __restrict__ embed, int vocab,
                                                      const int32_t* __restrict__ ids, int M, float* __restrict__ x,
-                                                     unsigned long long* __restrict__ slots) {
+                                                     unsigned long long* __restrict__ slots,
+                                                     const float* __restrict__ norm_w, int NT,
+                                                     uint16_t* __restrict__ act, float* __restrict__ ss, int ss_ld) {
+  __shared__ float red[4];
   grid_dep_wait();
   grid_dep_launch();
   const int t = blockIdx.x;
   int id = ids[t];
   if (id < 0 || id >= vocab) id = 0;  // ids are validated on the host; stay in bounds regardless
   const int cc = threadIdx.x;
+  float sq = 0.f;
   if (cc < kHidden / 8) {
     const int k = cc * 8;
     const uint4 w = *reinterpret_cast<const uint4*>(embed + tiled_offset(id, k, kHidden));
+    float e[8] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y),
+                  bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w)};
     float4* o = reinterpret_cast<float4*>(x + (long long)t * kHidden + k);
-    o[0] = make_float4(bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y));
-    o[1] = make_float4(bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w));
+    o[0] = make_float4(e[0], e[1], e[2], e[3]);
+    o[1] = make_float4(e[4], e[5], e[6], e[7]);
+    if (act) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        sq = fmaf(e[i], e[i], sq);
+        sq = fmaf(e[i + 1], e[i + 1], sq);
+        const float v0 = e[i] * norm_w[k + i], v1 = e[i + 1] * norm_w[k + i + 1];
+        const uint16_t h0 = f32_to_bf16_rn(v0), h1 = f32_to_bf16_rn(v1);
+        const uint16_t l0 = f32_to_bf16_rn(v0 - bf16_to_f32(h0)), l1 = f32_to_bf16_rn(v1 - bf16_to_f32(h1));
+        hw[i / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        lw[i / 2] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+      }
+      // one core-matrix row: 8 consecutive columns, 16 contiguous bytes per half
+      *reinterpret_cast<uint4*>(act + act_offset(t, k, 0, kHidden, NT)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(act + act_offset(t, k, 1, kHidden, NT)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
   }
   if (slots && threadIdx.x == 0) slots[t] = 0ull;
+  if (act && ss) {
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x < kHidden / 128)
+      ss[(long long)threadIdx.x * ss_ld + t] = threadIdx.x == 0 ? (red[0] + red[1]) + (red[2] + red[3]) : 0.f;
+  }
 }
 
 // KVCache.move_row (qweninfer/engine/kv_cache.py:65-73): for every (layer, K/V, head),
@@ -49,7 +81,8 @@ __global__ void __launch_bounds__(256) move_rows_kernel(uint16_t* __restrict__ k
 }  // namespace
 
 cudaError_t launch_embed(const uint16_t* embed, int vocab, const int32_t* ids, int M, float* x,
-                         unsigned long long* slots, cudaStream_t stream, bool pdl) {
+                         unsigned long long* slots, cudaStream_t stream, bool pdl, const float* norm_w, int NT,
+                         uint16_t* act, float* ss, int ss_ld) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M, 1, 1);
   cfg.blockDim = dim3(128, 1, 1);
@@ -59,7 +92,7 @@ cudaError_t launch_embed(const uint16_t* embed, int vocab, const int32_t* ids, i
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, embed_kernel, embed, vocab, ids, M, x, slots);
+  return cudaLaunchKernelEx(&cfg, embed_kernel, embed, vocab, ids, M, x, slots, norm_w, NT, act, ss, ss_ld);
 }
 
 cudaError_t launch_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_rows, int max_len,

@@ -1,0 +1,82 @@
+// Tensor-core projection kernel (tc_proj.cu) and the activation-tile format it consumes.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qi {
+
+enum TcEpilogue : int {
+  kTcPlain = 0,     // out[t, n] = rinv[t] * D[n, t]
+  kTcQkvRope = 1,   // bias + RoPE; q -> fp32, k/v -> bf16 cache
+  kTcResidual = 2,  // x[t, n] += D; next activations hi/lo(w_next * x) + sum-of-squares partials
+  kTcSwiglu = 3,    // h = silu(gate) * up -> activation tiles of the down projection
+  kTcLogits = 4,    // optional logits + packed argmax of the head tokens
+};
+
+// Activation tiles: for inner size K and token tile NT (8..128, power of two), token t,
+// column k, half `part` (0 = hi = bf16(x), 1 = lo = bf16(x - hi)):
+//   [t / NT][k / 64][part][(t % NT) / 8][(k % 64) / 8][t % 8][k % 8]   (bf16 elements)
+// One (token tile, 64-column block) is NT * 256 contiguous bytes: the B operand of one
+// pipeline stage, in the SWIZZLE_NONE K-major canonical layout.
+__host__ __device__ __forceinline__ long long act_offset(int t, int k, int part, int K, int NT) {
+  const int nt = t / NT, tl = t - nt * NT;
+  return ((long long)nt * (K / 64) + (k >> 6)) * (2LL * NT * 64) + (long long)part * NT * 64 +
+         (long long)(tl >> 3) * 512 + ((k & 63) >> 3) * 64 + (tl & 7) * 8 + (k & 7);
+}
+
+struct TcParams {
+  // A: weights (tiled), B: activation tiles
+  const uint16_t* w;
+  int KB;          // 64-column blocks of K
+  int n_mtiles;    // weight rows / 128
+  const uint16_t* act_in;
+  int NT;          // token tile
+  int n_ntiles;    // token tiles processed by this launch
+  int ntile0;      // first token tile
+  int M;           // live tokens (t >= M are padding)
+  const float* ss_in;  // (7, ss_ld) per-128-feature partial sums of squares, or null
+  int ss_ld;
+  float eps;
+  int epi;
+  // plain
+  float* out;
+  int out_ld;
+  // qkv
+  const float* bias;
+  const float* rope_cos;
+  const float* rope_sin;
+  const int32_t* pos;
+  const int32_t* rows;
+  float* q;
+  uint16_t* kc;
+  uint16_t* vc;
+  int max_len;
+  // residual / swiglu
+  float* x;
+  const float* next_norm_w;
+  float* ss_out;
+  uint16_t* act_out;
+  // logits: head tokens t = head_lo + i * head_stride (i < ...), t < head_hi
+  void* logits;
+  int logits_bf16;
+  long long logits_ld;
+  unsigned long long* argmax;
+  int head_lo, head_hi, head_stride;
+  // stream-K
+  float* scratch;          // gridDim.x * 2 * 128 * NT floats
+  unsigned int* counters;  // one per (m-tile, token tile), zero between launches
+  int stages;
+  uint32_t tmem_cols;
+  int* err;
+};
+
+size_t tc_proj_smem(int NT, int stages);
+cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, bool pdl);
+
+// x (M, K) fp32 -> activation tiles of (norm_w * x) (norm_w may be null) and, if ss is
+// non-null, per-token sums of squares of x in ss[0][t] (ss[1..6][t] = 0; K must be 896).
+cudaError_t launch_act_tiles(const float* x, const float* norm_w, int M, int K, int NT, uint16_t* act, float* ss,
+                             int ss_ld, cudaStream_t stream, bool pdl);
+
+}  // namespace qi

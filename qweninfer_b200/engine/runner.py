@@ -68,15 +68,15 @@ class DecodeRunner:
         self.launches = 0
         self.h2d_bytes = 0
         self.d2h_bytes = 0
-        self.kernels_per_forward = lambda n_head: 1 + 5 * model.cfg.num_hidden_layers + -(-n_head // 8)
+        self.kernels_per_forward = lambda n_head: 1 + 5 * model.cfg.num_hidden_layers + 1
 
     # ------------------------------------------------------------ helpers
 
-    def _forward(self, st: _Staging, M: int, ws, head_ptr, n_head: int) -> None:
+    def _forward(self, st: _Staging, M: int, ws, head_lo: int, n_head: int) -> None:
         self.launches += self.kernels_per_forward(n_head)
         _lib.check(_lib.lib().qi_forward(
             C.byref(self.model.native()), C.byref(self.cache.native()), C.byref(ws.struct),
-            st.ptr(0), st.ptr(1), st.ptr(2), M, head_ptr, n_head, None, 0, 0,
+            st.ptr(0), st.ptr(1), st.ptr(2), M, head_lo, 1, n_head, None, 0, 0,
             self.d_slots.data_ptr(), _lib.stream_ptr(self.dev)), "qi_forward")
 
     def _read(self, k: int) -> np.ndarray:
@@ -107,7 +107,7 @@ class DecodeRunner:
         self.pre.put(prompt, np.arange(P), np.full(P, row), head=P - 1)
         self.h2d_bytes += self.pre.h.numel() * 4
         ws = self.model.workspace(self.cache.max_len, self.cache.max_len).plan(P)
-        self._forward(self.pre, P, ws, self.pre.ptr(3), 1)
+        self._forward(self.pre, P, ws, P - 1, 1)
         return int(self._read(1)[0])
 
     @torch.inference_mode()
@@ -129,11 +129,11 @@ class DecodeRunner:
             g.replay()
         else:
             self.ws.plan(B)
-            self._forward(self.dec, B, self.ws, None, B)
+            self._forward(self.dec, B, self.ws, 0, B)
             if self.cuda_graphs:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
-                    self._forward(self.dec, B, self.ws, None, B)
+                    self._forward(self.dec, B, self.ws, 0, B)
                 self.graphs[B] = g
         self.steps += 1
         return self._read(B)

@@ -280,11 +280,25 @@ class _AttnScratch:
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
 
 
+def token_tile(M: int) -> int:
+    """Token tile of the tensor-core projections: power of two >= M, between 8 and 128."""
+    nt = 8
+    while nt < M and nt < 128:
+        nt *= 2
+    return nt
+
+
+def use_tensor_cores() -> bool:
+    """tcgen05 projections (default) or the CUDA-core GEMV path (QI_TENSOR_CORES=0)."""
+    import os
+    return os.environ.get("QI_TENSOR_CORES", "1") != "0"
+
+
 class Workspace:
     """Activation buffers and scratch of `qi_forward` for up to `max_tokens` tokens of a
     cache with `max_len` slots per row. The library never allocates; this does, once."""
 
-    def __init__(self, max_tokens: int, max_len: int, device: torch.device) -> None:
+    def __init__(self, max_tokens: int, max_len: int, device: torch.device, vocab: int = 151936) -> None:
         f32 = dict(dtype=torch.float32, device=device)
         self.max_tokens, self.max_len = max_tokens, max_len
         self.x = torch.empty(max_tokens, HIDDEN, **f32)
@@ -298,10 +312,24 @@ class Workspace:
         self.attn_part = torch.empty(parts, **f32)
         self.attn_counters = torch.zeros(max_tokens * 2, dtype=torch.int32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
-        self.struct = _lib.QiWorkspace(self.x.data_ptr(), self.q.data_ptr(), self.attn.data_ptr(),
-                                       self.h.data_ptr(), self.attn_part.data_ptr(),
-                                       self.attn_counters.data_ptr(), max_tokens, 1, 128,
-                                       self.err.data_ptr())
+        # tensor-core path: activation tiles (hi/lo bf16), sums of squares, stream-K scratch
+        nt = token_tile(max_tokens)
+        pad = -(-max_tokens // nt) * nt
+        bf = dict(dtype=torch.bfloat16, device=device)
+        self.act_x = torch.zeros(pad * HIDDEN * 2, **bf)
+        self.act_attn = torch.zeros(pad * HIDDEN * 2, **bf)
+        self.act_h = torch.zeros(pad * INTER * 2, **bf)
+        self.ss = torch.zeros(7 * pad, **f32)
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        self.tc_scratch = torch.empty(sms * 2 * 128 * nt, **f32)
+        n_counters = max(76 * (pad // nt), -(-vocab // 128), 64)
+        self.tc_counters = torch.zeros(n_counters, dtype=torch.int32, device=device)
+        self.struct = _lib.QiWorkspace(
+            self.x.data_ptr(), self.q.data_ptr(), self.attn.data_ptr(), self.h.data_ptr(),
+            self.attn_part.data_ptr(), self.attn_counters.data_ptr(), max_tokens, 1, 128, self.err.data_ptr(),
+            int(use_tensor_cores()), self.act_x.data_ptr(), self.act_attn.data_ptr(), self.act_h.data_ptr(),
+            self.ss.data_ptr(), pad, self.tc_scratch.data_ptr(), self.tc_scratch.numel(),
+            self.tc_counters.data_ptr(), n_counters)
 
     def plan(self, M: int) -> "Workspace":
         self.struct.split_keys, self.struct.max_splits = _split_plan(M, self.max_len)
@@ -397,7 +425,7 @@ class Qwen2(nn.Module):
         key = (max_tokens, max_len)
         ws = self._workspaces.get(key)
         if ws is None:
-            ws = Workspace(max_tokens, max_len, self.device)
+            ws = Workspace(max_tokens, max_len, self.device, self.cfg.vocab_size)
             self._workspaces[key] = ws
         return ws
 
@@ -437,19 +465,17 @@ class Qwen2(nn.Module):
         dev = self.device
         B, S = input_ids.shape
         cache, M, ids32, pos32, rows32 = self._inputs(input_ids, positions, cache)
-        n_head = B if last_only else M
-        head = None
-        if last_only and S > 1:
-            head = (torch.arange(B, device=dev, dtype=torch.int32) * S + (S - 1)).contiguous()
+        # head tokens: every token, or the last of each sequence (b*S + S-1)
+        n_head, head_lo, head_stride = (B, S - 1, S) if last_only else (M, 0, 1)
         ldt = logits_dtype or self.dtype
         if ldt not in (torch.float32, torch.bfloat16):
             raise ValueError("logits are produced in float32 or bfloat16")
         logits = torch.empty(n_head, self.cfg.vocab_size, dtype=ldt, device=dev)
-        slots = torch.empty(M, dtype=torch.int64, device=dev)
+        slots = torch.zeros(M, dtype=torch.int64, device=dev)
         ws = self.workspace(max(M, 1), cache.max_len).plan(M)
         _lib.check(_lib.lib().qi_forward(
             C.byref(self.native()), C.byref(cache.native()), C.byref(ws.struct), ids32.data_ptr(),
-            pos32.data_ptr(), rows32.data_ptr(), M, _lib.ptr(head), n_head, logits.data_ptr(),
+            pos32.data_ptr(), rows32.data_ptr(), M, head_lo, head_stride, n_head, logits.data_ptr(),
             int(ldt == torch.bfloat16), self.cfg.vocab_size, slots.data_ptr(), _lib.stream_ptr(dev)),
             "qi_forward")
         self.last_argmax = self.decode_argmax(slots[:n_head])
@@ -476,7 +502,7 @@ class Qwen2(nn.Module):
             return ws.x[:M].clone().view(B, S, HIDDEN)
         _lib.check(_lib.lib().qi_forward(
             C.byref(part), C.byref(cache.native()), C.byref(ws.struct), ids32.data_ptr(), pos32.data_ptr(),
-            rows32.data_ptr(), M, None, 0, None, 0, 0, None, _lib.stream_ptr(self.device)), "qi_forward")
+            rows32.data_ptr(), M, 0, 1, 0, None, 0, 0, None, _lib.stream_ptr(self.device)), "qi_forward")
         return ws.x[:M].clone().view(B, S, HIDDEN)
 
     @staticmethod

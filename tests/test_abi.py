@@ -65,7 +65,17 @@ def test_host_argument_checks_reject_before_launch(lib):
     long = (C.c_int * 3)(0, 1, 65)
     assert lib.qi_move_rows(1, 1, 2, 4, 64, long, 1, None) == E
     # forward: null descriptors
-    assert lib.qi_forward(None, None, None, 1, 1, 1, 1, None, 0, None, 0, 0, None, None) == E
+    assert lib.qi_forward(None, None, None, 1, 1, 1, 1, 0, 1, 0, None, 0, 0, None, None) == E
+    # tensor-core blocks: token tile must be a power of two in 8..128, rows % 128, K % 64
+    assert lib.qi_act_tiles(1, None, 4, 896, 12, 1, None, 0, None) == E
+    assert lib.qi_act_tiles(1, None, 4, 100, 8, 1, None, 0, None) == E
+    assert lib.qi_tc_linear(1, 1000, 896, 1, 4, 8, None, 0, C.c_float(0), 1, 1000, 1, 10**6, 1, 64, 0, 1,
+                            None) == E
+    assert lib.qi_tc_linear(1, 1024, 896, 1, 4, 256, None, 0, C.c_float(0), 1, 1024, 1, 10**6, 1, 64, 0, 1,
+                            None) == E
+    # too few tile counters for 8 m-tiles
+    assert lib.qi_tc_linear(1, 1024, 896, 1, 4, 8, None, 0, C.c_float(0), 1, 1024, 1, 10**6, 1, 4, 0, 1,
+                            None) == E
 
 
 def test_cpu_tensors_are_refused():
