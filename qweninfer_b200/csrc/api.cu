@@ -185,11 +185,25 @@ int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* c
   stages = stages < 2 ? 2 : (stages > 8 ? 8 : stages);
   uint32_t cols = 32;
   while (cols < (uint32_t)(4 * p.NT)) cols <<= 1;
+  p.lg_nt = 0;
+  while ((1 << p.lg_nt) < p.NT) ++p.lg_nt;
   p.scratch = scratch;
   p.counters = counters;
   p.stages = stages;
   p.tmem_cols = cols;
   return rc(launch_tc_proj(p, g, s, pdl));
+}
+
+// Stream-K grid of a projection with n_tiles output tiles of KB k-blocks each: enough
+// contributors per tile to cover the SMs, but at most max_contrib, because the last
+// contributor of a split tile reads every other contributor's partial.
+int grid_for(int n_tiles, int KB, int max_contrib) {
+  const int sms = sm_count();
+  int per = (sms + n_tiles - 1) / n_tiles;
+  if (per > max_contrib) per = max_contrib;
+  if (per > KB) per = KB;
+  const long long g = (long long)n_tiles * per;
+  return (int)(g < sms ? g : sms);
 }
 
 // qi_forward on the tensor-core path: every projection is a tc_proj launch whose
@@ -214,8 +228,9 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
   base.ss_ld = ws->ss_ld;
   base.eps = model->eps;
   base.err = ws->err;
-  auto launch = [&](TcParams& p) {
-    return run_tc(p, ws->tc_scratch, ws->tc_scratch_floats, ws->tc_counters, ws->tc_counters_len, 0, s, pdl);
+  auto launch = [&](TcParams& p, int max_contrib) {
+    const int g = grid_for(p.n_mtiles * p.n_ntiles, p.KB, max_contrib);
+    return run_tc(p, ws->tc_scratch, ws->tc_scratch_floats, ws->tc_counters, ws->tc_counters_len, g, s, pdl);
   };
   const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
   for (int li = 0; li < model->num_layers; ++li) {
@@ -238,7 +253,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.kc = kl;
     p.vc = vl;
     p.max_len = cache->max_len;
-    if ((r = launch(p)) != QI_OK) return r;
+    if ((r = launch(p, 8)) != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
                   ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, NT);
     if (r != QI_OK) return r;
@@ -252,7 +267,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.next_norm_w = L.ln2;
     p.act_out = ws->act_x;
     p.ss_out = ws->ss;
-    if ((r = launch(p)) != QI_OK) return r;
+    if ((r = launch(p, 8)) != QI_OK) return r;
     p = base;  // gate/up + SwiGLU
     p.w = L.w_gate_up;
     p.KB = kHidden / 64;
@@ -261,7 +276,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.ss_in = ws->ss;
     p.epi = kTcSwiglu;
     p.act_out = ws->act_h;
-    if ((r = launch(p)) != QI_OK) return r;
+    if ((r = launch(p, 148)) != QI_OK) return r;
     p = base;  // down + residual; emits the next norm's inputs
     p.w = L.w_down;
     p.KB = kInter / 64;
@@ -272,7 +287,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.next_norm_w = li + 1 < model->num_layers ? model->layers[li + 1].ln1 : model->norm;
     p.act_out = ws->act_x;
     p.ss_out = ws->ss;
-    if ((r = launch(p)) != QI_OK) return r;
+    if ((r = launch(p, 12)) != QI_OK) return r;
   }
   if (n_head > 0) {
     const int head_hi = head_lo + (n_head - 1) * head_stride + 1;
@@ -293,7 +308,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
       p.head_lo = head_lo;
       p.head_hi = head_hi;
       p.head_stride = head_stride;
-      if ((r = launch(p)) != QI_OK) return r;
+      if ((r = launch(p, 148)) != QI_OK) return r;
     }
   }
   return QI_OK;

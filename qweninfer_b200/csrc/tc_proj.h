@@ -32,6 +32,7 @@ struct TcParams {
   int n_mtiles;    // weight rows / 128
   const uint16_t* act_in;
   int NT;          // token tile
+  int lg_nt;       // log2(NT)
   int n_ntiles;    // token tiles processed by this launch
   int ntile0;      // first token tile
   int M;           // live tokens (t >= M are padding)

@@ -25,6 +25,10 @@ pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 
 TIGHT_ATOL = 5e-3       # vs the oracle with a bf16 cache (same storage rounding as the GPU)
 CACHE_TOL = 1e-3        # cached vs full recompute, batched vs alone (test_cache.py:20)
+# residual stream vs the bf16-cache oracle, relative to the layer's largest value: fp32
+# reassociation drifts smoothly with depth (~1e-3 after 24 layers); a wrong kernel shows
+# up as O(1) error in one layer
+HIDDEN_RTOL = 3e-3
 
 
 @pytest.fixture(scope="module")
@@ -102,7 +106,7 @@ def test_hidden_states_per_layer(gpu_model, oracle_bf16w, g0, full_cfg):
         ref = hidden[n][0]
         rel = np.abs(got - ref).max() / np.abs(ref).max()
         lines.append(f"layer {n}: rel {rel:.2e}")
-        if first_bad is None and rel > 1e-3:
+        if first_bad is None and rel > HIDDEN_RTOL:
             first_bad = n
     assert first_bad is None, "\n".join(lines)
     # the reference's own per-layer values at positions 0 and 63 (fp32 cache)
