@@ -35,6 +35,7 @@ extern "C" {
 #define QI_ERR_ARG 1001     /* an argument is out of range                          */
 #define QI_ERR_TIMEOUT 1002 /* a device-side bounded wait gave up (set in *err)      */
 #define QI_ERR_DEVICE 1003  /* the current device is not an sm_100 part              */
+#define QI_ERR_TOO_LARGE 1004 /* size beyond a fixed-capacity entry point's maximum  */
 
 typedef void* qi_stream_t; /* cudaStream_t */
 
@@ -99,6 +100,22 @@ int qi_attention(const float* q, const uint16_t* k_layer, const uint16_t* v_laye
                  const int32_t* pos, const int32_t* rows, int M, int max_len, int split_keys,
                  int max_splits, float* out, float* part, unsigned int* counters, int* err,
                  qi_stream_t stream);
+
+/* Attention as qi_attention, for callers that cannot allocate device memory (a host
+ * program binding this C ABI directly that only holds device pointers to its own
+ * tensors, or a process whose device memory is fixed at start-up): the split partials
+ * and arrival counters live in a static array inside the library (~3.6 MiB on every GPU
+ * that loads it, held until the process exits) instead of caller-provided scratch. The
+ * caller passes only inputs and outputs; `out` is fp32 (M, 896), `err` may be NULL.
+ * Limits: M <= 64 query tokens and max_len <= 2048 cache slots per row; larger sizes
+ * return QI_ERR_TOO_LARGE before anything is enqueued. The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) and should come before any stream
+ * capture. Calls share the array: calls whose executions overlap on the GPU (different
+ * streams or threads) race and give wrong results; calls in one stream are safe.
+ * No counterpart in the reference (its attention allocates through PyTorch). */
+int qi_attention_noalloc(const float* q, const uint16_t* k_layer, const uint16_t* v_layer,
+                         const int32_t* pos, const int32_t* rows, int M, int max_len, float* out,
+                         int* err, qi_stream_t stream);
 
 /* o_proj + residual add into the fp32 stream:  x[t] += attn[t] @ Wo^T.
  * Replaces qweninfer/models/qwen2.py:203-204 and the residual add of 237-238.

@@ -19,6 +19,7 @@ QI_OK = 0
 QI_ERR_ARG = 1001
 QI_ERR_TIMEOUT = 1002
 QI_ERR_DEVICE = 1003
+QI_ERR_TOO_LARGE = 1004
 
 vp = C.c_void_p
 i32 = C.c_int
@@ -57,6 +58,7 @@ SIGNATURES = {
     "qi_embed": (i32, [vp, i32, vp, i32, vp, vp, vp, vp]),
     "qi_qkv_rope_append": (i32, [vp, vp, f32, vp, vp, vp, vp, vp, vp, i32, vp, vp, i32, vp, vp, vp]),
     "qi_attention": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
+    "qi_attention_noalloc": (i32, [vp, vp, vp, vp, vp, i32, i32, vp, vp, vp]),
     "qi_o_proj_residual": (i32, [vp, vp, i32, vp, vp, vp]),
     "qi_gate_up_swiglu": (i32, [vp, vp, f32, vp, i32, vp, vp, vp]),
     "qi_down_residual": (i32, [vp, vp, i32, vp, vp, vp]),
@@ -102,7 +104,8 @@ def lib() -> C.CDLL:
 def check(code: int, what: str) -> None:
     if code != QI_OK:
         names = {QI_ERR_ARG: "invalid argument", QI_ERR_TIMEOUT: "device wait timed out",
-                 QI_ERR_DEVICE: "not an sm_100 (B200) device"}
+                 QI_ERR_DEVICE: "not an sm_100 (B200) device",
+                 QI_ERR_TOO_LARGE: "size beyond the entry point's fixed capacity"}
         raise QiError(f"{what} failed: {names.get(code, f'CUDA error {code}')}")
 
 

@@ -9,6 +9,8 @@
 // and accumulate P.V with lane = 2 output dims. Warps and splits are merged with the
 // usual max-rescaled sums; the last CTA of a token/head (atomic arrival count) merges
 // the splits in split order and resets its counter.
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 #include "tc_proj.h"
@@ -257,4 +259,83 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl)
   return cudaLaunchKernelEx(&cfg, attention_kernel, p);
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Attention without caller-provided scratch.
+//
+// Some callers of this library cannot allocate device memory: a host program that binds
+// the C ABI directly (C, Go, Java, ...) and only receives device pointers for the tensors
+// it owns, or a serving process whose device memory is reserved once at start-up and must
+// not grow afterwards. For them, the split partials and arrival counters of the attention
+// kernel live in this file-scope array instead, so the call takes only inputs and outputs.
+//
+// Capacity: up to kNoAllocMaxTokens query tokens and kNoAllocMaxLen cache slots per row
+// (128-key splits). The array (about 3.6 MiB) is part of the library image, so every GPU
+// that loads libqi.so holds it until the process exits. All calls share it: two calls whose
+// executions overlap on the GPU (other streams, other threads) race on it and give wrong
+// results; calls in one stream are ordered and safe.
+namespace {
+constexpr int kNoAllocMaxTokens = 64;
+constexpr int kNoAllocMaxLen = 2048;
+constexpr int kNoAllocSplitKeys = 128;
+constexpr int kNoAllocMaxSplits = kNoAllocMaxLen / kNoAllocSplitKeys;
+constexpr size_t kNoAllocPartWords = (size_t)kNoAllocMaxTokens * kKvHeads * kNoAllocMaxSplits * kPartStride;
+constexpr size_t kNoAllocCounterWords = (size_t)kNoAllocMaxTokens * kKvHeads;
+}  // namespace
+
+// partials (fp32) followed by the arrival counters (uint32)
+static __device__ __align__(256) unsigned int g_attn_noalloc_scratch[kNoAllocPartWords + kNoAllocCounterWords];
+
+namespace {
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[64] = {};  // device address of the array, per device ordinal
+}  // namespace
+
 }  // namespace qi
+
+extern "C" int qi_attention_noalloc(const float* q, const uint16_t* k_layer, const uint16_t* v_layer,
+                                    const int32_t* pos, const int32_t* rows, int M, int max_len, float* out,
+                                    int* err, qi_stream_t stream) {
+  using namespace qi;
+  if (M > kNoAllocMaxTokens || max_len > kNoAllocMaxLen) return QI_ERR_TOO_LARGE;
+  if (M <= 0 || max_len <= 0 || !q || !k_layer || !v_layer || !pos || !rows || !out) return QI_ERR_ARG;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= 64) return QI_ERR_ARG;
+  void* base = nullptr;
+  {
+    // first call on this device: resolve the array's device address (host code must not
+    // use the symbol itself, which names a host-side stand-in)
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_addr[dev]) {
+      e = cudaGetSymbolAddress(&g_noalloc_addr[dev], g_attn_noalloc_scratch);
+      if (e != cudaSuccess) {
+        g_noalloc_addr[dev] = nullptr;
+        return (int)e;
+      }
+    }
+    base = g_noalloc_addr[dev];
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  unsigned int* counters = static_cast<unsigned int*>(base) + kNoAllocPartWords;
+  // the counters must start at zero; the array keeps whatever the previous call left
+  e = cudaMemsetAsync(counters, 0, kNoAllocCounterWords * sizeof(unsigned int), s);
+  if (e != cudaSuccess) return (int)e;
+  AttnParams a = {};
+  a.q = q;
+  a.kc = k_layer;
+  a.vc = v_layer;
+  a.pos = pos;
+  a.rows = rows;
+  a.M = M;
+  a.max_len = max_len;
+  a.split_keys = kNoAllocSplitKeys;
+  a.max_splits = (max_len + kNoAllocSplitKeys - 1) / kNoAllocSplitKeys;
+  a.out = out;
+  a.part = static_cast<float*>(base);
+  a.counters = counters;
+  a.err = err;
+  e = launch_attention(a, s, false);
+  return e == cudaSuccess ? QI_OK : (int)e;
+}
