@@ -3,6 +3,7 @@
 // Host-side argument checks and launch planning live here; the kernels are in
 // gemv.cu, attention.cu and misc.cu. Nothing here allocates device memory.
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -169,8 +170,21 @@ inline int token_tile(int M) {
   return nt;
 }
 
+// Shared-memory budget of a tensor-core projection CTA for its pipeline stages, in KB
+// (QI_TC_SMEM_KB overrides the default of 144 for tuning experiments; 144 KB measured best
+// across decode batches 1-64 and prefill, see profiles/).
+int tc_smem_budget_kb() {
+  static int kb = -1;
+  if (kb < 0) {
+    const char* s = getenv("QI_TC_SMEM_KB");
+    const int v = s ? atoi(s) : 0;
+    kb = (v >= 48 && v <= 220) ? v : 144;
+  }
+  return kb;
+}
+
 // Plan and launch one tensor-core projection: grid = min(SMs, units, scratch capacity),
-// pipeline stages within a ~100 KB shared-memory budget, TMEM for two accumulators.
+// pipeline stages within the shared-memory budget, TMEM for two accumulators.
 int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* counters, int counters_len,
            int ctas, cudaStream_t s, bool pdl) {
   const long long units = (long long)p.n_mtiles * p.n_ntiles * p.KB;
@@ -180,9 +194,11 @@ int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* c
   const long long per_cta = 2LL * 128 * p.NT;
   if (scratch_floats / per_cta < g) g = (int)(scratch_floats / per_cta);
   if (g < 1) return QI_ERR_ARG;
+  // Deep pipelines: a CTA streams at (bytes in flight) / (loaded DRAM latency, ~3 us), so
+  // ~130 KB must be in flight per SM to reach the HBM rate.
   const size_t stage = 16384 + (size_t)p.NT * 256;
-  int stages = (int)((100 * 1024) / stage);
-  stages = stages < 2 ? 2 : (stages > 8 ? 8 : stages);
+  int stages = (int)((size_t)tc_smem_budget_kb() * 1024 / stage);
+  stages = stages < 2 ? 2 : (stages > 12 ? 12 : stages);
   uint32_t cols = 32;
   while (cols < (uint32_t)(4 * p.NT)) cols <<= 1;
   p.lg_nt = 0;
