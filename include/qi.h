@@ -36,6 +36,8 @@ extern "C" {
 #define QI_ERR_TIMEOUT 1002 /* a device-side bounded wait gave up (set in *err)      */
 #define QI_ERR_DEVICE 1003  /* the current device is not an sm_100 part              */
 #define QI_ERR_TOO_LARGE 1004 /* size beyond a fixed-capacity entry point's maximum  */
+#define QI_ERR_INDEX 1005   /* a token's position or cache row lies outside the cache
+                               (set in *err by the kernels; the access is skipped)  */
 
 typedef void* qi_stream_t; /* cudaStream_t */
 
@@ -211,6 +213,13 @@ typedef struct {
   long long tc_scratch_floats;
   unsigned int* tc_counters;/* one per output tile, zero-initialised          */
   int tc_counters_len;
+  /* persistent forward (qi_persistent_launch) */
+  unsigned int* persist_done; /* completion counters, 32 uints (one 128-byte line)
+                                 per stage: persist_done_len >= 32 * stages        */
+  int persist_done_len;
+  unsigned long long* persist_trace; /* optional (may be NULL): stages + 1 globaltimer
+                                        stamps (ns): each stage's finish, then the
+                                        launch's start at [n_stages]                   */
 } qi_workspace;
 
 /* Full Qwen2 forward of M tokens (qweninfer/models/qwen2.py:263-292 with a cache):
@@ -227,6 +236,27 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
                const int32_t* ids, const int32_t* pos, const int32_t* rows, int M, int head_lo,
                int head_stride, int n_head, void* logits, int logits_bf16, long long logits_ld,
                unsigned long long* argmax_slots, qi_stream_t stream);
+
+/* ------------------------------------------------------- persistent forward */
+
+/* The forward of qi_forward as ONE cooperative launch for M <= 128 tokens (a decode step
+ * or a short prefill): 148 resident CTAs walk a stage table (embed, 24 x {QKV,
+ * attention, o, gate/up, down}, head); each CTA streams its weight blocks ahead across
+ * stage boundaries while activations follow global completion counters. Same arguments
+ * and results as qi_forward (tensor-core path).
+ * qi_persistent_plan writes the stage table into host memory (table_bytes >= 200 KB is
+ * ample; qi_persistent_stage_bytes() per stage) for the caller to copy to device memory;
+ * the table depends only on the pointers and sizes given, so it can be reused by every
+ * launch with the same buffers. qi_persistent_launch zeroes ws->persist_done and
+ * launches. */
+long long qi_persistent_stage_bytes(void);
+int qi_persistent_plan(const qi_model* model, const qi_cache* cache, const qi_workspace* ws,
+                       const int32_t* ids, const int32_t* pos, const int32_t* rows, int M,
+                       int head_lo, int head_stride, int n_head, void* logits, int logits_bf16,
+                       long long logits_ld, unsigned long long* argmax_slots, void* host_table,
+                       long long table_bytes, int* n_stages);
+int qi_persistent_launch(const void* device_table, int n_stages, const qi_workspace* ws, int M,
+                         qi_stream_t stream);
 
 /* ------------------------------------------------- tensor-core building blocks */
 

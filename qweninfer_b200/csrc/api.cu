@@ -4,10 +4,14 @@
 // gemv.cu, attention.cu and misc.cu. Nothing here allocates device memory.
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "internal.h"
 #include "tc_proj.h"
+#include "persistent.h"
+
+#include <vector>
 
 using namespace qi;
 
@@ -76,7 +80,9 @@ int qkv(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv, con
 
 int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int32_t* pos, const int32_t* rows,
               int M, int max_len, int split_keys, int max_splits, float* out, float* part, unsigned int* counters,
-              int* err, cudaStream_t s, bool pdl, uint16_t* out_act = nullptr, int out_nt = 0) {
+              int* err, cudaStream_t s, bool pdl, uint16_t* out_act = nullptr, int out_nt = 0,
+              int cache_rows = 0) {
+  if (max_splits > kMaxAttnSplits) return QI_ERR_ARG;
   AttnParams a = {};
   a.out_act = out_act;
   a.out_nt = out_nt;
@@ -87,6 +93,7 @@ int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int3
   a.rows = rows;
   a.M = M;
   a.max_len = max_len;
+  a.cache_rows = cache_rows;
   a.split_keys = split_keys;
   a.max_splits = max_splits;
   a.out = out;
@@ -234,7 +241,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
       !ws->tc_counters)
     return QI_ERR_ARG;
   const bool pdl = true;
-  int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, slots, s, false, model->layers[0].ln1, NT,
+  int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, slots, n_head, s, false, model->layers[0].ln1, NT,
                           ws->act_x, ws->ss, ws->ss_ld));
   if (r != QI_OK) return r;
   TcParams base = {};
@@ -269,9 +276,10 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.kc = kl;
     p.vc = vl;
     p.max_len = cache->max_len;
+    p.cache_rows = cache->cache_rows;
     if ((r = launch(p, 8)) != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
-                  ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, NT);
+                  ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, NT, cache->cache_rows);
     if (r != QI_OK) return r;
     p = base;  // o_proj + residual; emits RMSNorm(post_attention) inputs
     p.w = L.w_o;
@@ -330,9 +338,223 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
   return QI_OK;
 }
 
+// Stage table of the persistent forward (forward_persistent.cu): the same projections,
+// epilogues, attention and embedding as forward_tc, each with the CTA subset and
+// completion target it uses, and the stage it waits for.
+// Contributor caps of the persistent forward's projections (qkv, o, gate/up, down, head);
+// QI_PERSIST_CAPS="a,b,c,d,e" overrides them for sweeps.
+void persistent_caps(int caps[5]) {
+  static int cached[5] = {0, 0, 0, 0, 0};
+  if (!cached[0]) {
+    int v[5] = {8, 8, 148, 12, 148};
+    if (const char* e = getenv("QI_PERSIST_CAPS"))
+      sscanf(e, "%d,%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3], &v[4]);
+    for (int i = 0; i < 5; ++i) cached[i] = v[i] > 0 ? v[i] : 1;
+  }
+  for (int i = 0; i < 5; ++i) caps[i] = cached[i];
+}
+
+int plan_persistent(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
+                    const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
+                    void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots,
+                    std::vector<PStage>& out) {
+  const int NT = token_tile(M);
+  if (M > 128 || M > ws->ss_ld || !ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss || !ws->tc_scratch ||
+      !ws->tc_counters || !ws->err)
+    return QI_ERR_ARG;
+  int lg = 0;
+  while ((1 << lg) < NT) ++lg;
+  if (ws->tc_scratch_floats < (long long)sm_count() * 2 * 128 * NT) return QI_ERR_ARG;
+  TcParams base = {};
+  base.NT = NT;
+  base.lg_nt = lg;
+  base.n_ntiles = 1;
+  base.M = M;
+  base.ss_ld = ws->ss_ld;
+  base.eps = model->eps;
+  base.err = ws->err;
+  base.scratch = ws->tc_scratch;
+  base.counters = ws->tc_counters;
+  out.clear();
+  int caps[5];
+  persistent_caps(caps);
+  PStage e = {};
+  e.kind = kPEmbed;
+  e.dep = -1;
+  e.target = M;
+  e.tc = base;
+  e.em.table = model->embed;
+  e.em.vocab = model->vocab;
+  e.em.ids = ids;
+  e.em.norm_w = model->layers[0].ln1;
+  e.em.x = ws->x;
+  e.em.act = ws->act_x;
+  e.em.ss = ws->ss;
+  e.em.slots = slots;
+  e.em.n_slots = n_head;
+  out.push_back(e);
+  auto gemm = [&](const TcParams& p, int dep, int cap) {
+    PStage g = {};
+    g.kind = kPGemm;
+    g.dep = dep;
+    g.target = p.n_mtiles * p.n_ntiles;
+    g.ctas = grid_for(p.n_mtiles * p.n_ntiles, p.KB, cap);  // CTAs that take part
+    g.tc = p;
+    out.push_back(g);
+    return (int)out.size() - 1;
+  };
+  const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
+  int prev = 0;
+  for (int li = 0; li < model->num_layers; ++li) {
+    const qi_layer& L = model->layers[li];
+    uint16_t* kl = cache->k + li * layer_elems;
+    uint16_t* vl = cache->v + li * layer_elems;
+    TcParams p = base;
+    p.w = L.w_qkv;
+    p.KB = kHidden / 64;
+    p.n_mtiles = kQkvRows / 128;
+    p.act_in = ws->act_x;
+    p.ss_in = ws->ss;
+    p.epi = kTcQkvRope;
+    p.bias = L.b_qkv;
+    p.rope_cos = model->rope_cos;
+    p.rope_sin = model->rope_sin;
+    p.pos = pos;
+    p.rows = rows;
+    p.q = ws->q;
+    p.kc = kl;
+    p.vc = vl;
+    p.max_len = cache->max_len;
+    p.cache_rows = cache->cache_rows;
+    const int s_qkv = gemm(p, prev, caps[0]);
+    PStage a = {};
+    a.kind = kPAttn;
+    a.dep = s_qkv;
+    a.target = M * kKvHeads;
+    a.tc = base;
+    a.at.q = ws->q;
+    a.at.kc = kl;
+    a.at.vc = vl;
+    a.at.pos = pos;
+    a.at.rows = rows;
+    a.at.M = M;
+    a.at.max_len = cache->max_len;
+    a.at.cache_rows = cache->cache_rows;
+    a.at.split_keys = ws->split_keys;
+    a.at.max_splits = ws->max_splits;
+    a.at.out = nullptr;
+    a.at.out_act = ws->act_attn;
+    a.at.out_nt = NT;
+    a.at.part = ws->attn_part;
+    a.at.counters = ws->attn_counters;
+    a.at.err = ws->err;
+    out.push_back(a);
+    const int s_attn = (int)out.size() - 1;
+    p = base;
+    p.w = L.w_o;
+    p.KB = kHidden / 64;
+    p.n_mtiles = kHidden / 128;
+    p.act_in = ws->act_attn;
+    p.epi = kTcResidual;
+    p.x = ws->x;
+    p.next_norm_w = L.ln2;
+    p.act_out = ws->act_x;
+    p.ss_out = ws->ss;
+    const int s_o = gemm(p, s_attn, caps[1]);
+    p = base;
+    p.w = L.w_gate_up;
+    p.KB = kHidden / 64;
+    p.n_mtiles = kGateUpRows / 128;
+    p.act_in = ws->act_x;
+    p.ss_in = ws->ss;
+    p.epi = kTcSwiglu;
+    p.act_out = ws->act_h;
+    const int s_gu = gemm(p, s_o, caps[2]);
+    p = base;
+    p.w = L.w_down;
+    p.KB = kInter / 64;
+    p.n_mtiles = kHidden / 128;
+    p.act_in = ws->act_h;
+    p.epi = kTcResidual;
+    p.x = ws->x;
+    p.next_norm_w = li + 1 < model->num_layers ? model->layers[li + 1].ln1 : model->norm;
+    p.act_out = ws->act_x;
+    p.ss_out = ws->ss;
+    prev = gemm(p, s_gu, caps[3]);
+  }
+  if (n_head > 0) {
+    TcParams p = base;
+    p.w = model->embed;
+    p.KB = kHidden / 64;
+    p.n_mtiles = model->vocab / 128;
+    p.act_in = ws->act_x;
+    p.ss_in = ws->ss;
+    p.epi = kTcLogits;
+    p.logits = logits;
+    p.logits_bf16 = logits_bf16;
+    p.logits_ld = logits_ld;
+    p.argmax = slots;
+    p.head_lo = head_lo;
+    p.head_hi = head_lo + (n_head - 1) * head_stride + 1;
+    p.head_stride = head_stride;
+    gemm(p, prev, caps[4]);
+  }
+  return QI_OK;
+}
+
+int launch_persistent_table(const void* table, int n_stages, const qi_workspace* ws, int M, cudaStream_t s) {
+  if (!table || n_stages <= 0 || !ws || !ws->persist_done || (long long)n_stages * kDoneStride > ws->persist_done_len ||
+      M <= 0 || M > 128)
+    return QI_ERR_ARG;
+  PParams P = {};
+  P.stages = static_cast<const PStage*>(table);
+  P.n_stages = n_stages;
+  P.done = ws->persist_done;
+  P.M = M;
+  P.NT = token_tile(M);
+  P.ring = persistent_ring(P.NT);
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(4 * P.NT)) cols <<= 1;
+  P.tmem_cols = cols;
+  P.err = ws->err;
+  P.trace = ws->persist_trace;
+  cudaError_t e = cudaMemsetAsync(ws->persist_done, 0, sizeof(unsigned int) * kDoneStride * (size_t)n_stages, s);
+  if (e != cudaSuccess) return (int)e;
+  return rc(launch_persistent(P, sm_count(), s));
+}
+
 }  // namespace
 
 extern "C" {
+
+long long qi_persistent_stage_bytes(void) { return (long long)sizeof(PStage); }
+
+int qi_persistent_plan(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
+                       const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
+                       void* logits, int logits_bf16, long long logits_ld, unsigned long long* argmax_slots,
+                       void* host_table, long long table_bytes, int* n_stages) {
+  if (!model || !cache || !ws || !model->layers || !host_table || !n_stages || M <= 0 || n_head < 0 ||
+      (n_head > 0 && (head_lo < 0 || head_stride < 1 || (long long)head_lo + (long long)(n_head - 1) * head_stride >= M ||
+                      !argmax_slots)) ||
+      bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || (logits && logits_ld < model->vocab) ||
+      model->vocab % kTileRows != 0 || model->num_layers <= 0 || ws->split_keys % 128 != 0 ||
+      (long long)ws->split_keys * ws->max_splits < cache->max_len || ws->max_splits > kMaxAttnSplits)
+    return QI_ERR_ARG;
+  std::vector<PStage> st;
+  const int r = plan_persistent(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits,
+                                logits_bf16, logits_ld, argmax_slots, st);
+  if (r != QI_OK) return r;
+  if ((long long)(st.size() * sizeof(PStage)) > table_bytes) return QI_ERR_ARG;
+  memcpy(host_table, st.data(), st.size() * sizeof(PStage));
+  *n_stages = (int)st.size();
+  return QI_OK;
+}
+
+int qi_persistent_launch(const void* device_table, int n_stages, const qi_workspace* ws, int M, qi_stream_t stream) {
+  return launch_persistent_table(device_table, n_stages, ws, M, as_stream(stream));
+}
+
+
 
 int qi_version(void) { return kVersion; }
 
@@ -353,7 +575,7 @@ int qi_embed(const uint16_t* embed, int vocab, const int32_t* ids, int M, float*
              unsigned long long* argmax_slots, int* err, qi_stream_t stream) {
   (void)err;
   if (M <= 0 || vocab <= 0 || bad_ptr(embed) || bad_ptr(ids) || bad_ptr(x)) return QI_ERR_ARG;
-  return rc(launch_embed(embed, vocab, ids, M, x, argmax_slots, as_stream(stream), false));
+  return rc(launch_embed(embed, vocab, ids, M, x, argmax_slots, M, as_stream(stream), false));
 }
 
 int qi_qkv_rope_append(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv,
@@ -476,13 +698,13 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
       (n_head > 0 && (head_lo < 0 || head_stride < 1 || (long long)head_lo + (long long)(n_head - 1) * head_stride >= M)) ||
       bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || (n_head > 0 && bad_ptr(argmax_slots)) ||
       (logits && logits_ld < model->vocab) || model->vocab % kTileRows != 0 || model->num_layers <= 0 ||
-      ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len)
+      ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len || ws->max_splits > kMaxAttnSplits)
     return QI_ERR_ARG;
   if (ws->use_tc) return forward_tc(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits,
                                     logits_bf16, logits_ld, argmax_slots, as_stream(stream));
   cudaStream_t s = as_stream(stream);
   const bool pdl = true;
-  int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, argmax_slots, s, false));
+  int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, argmax_slots, n_head, s, false));
   if (r != QI_OK) return r;
   const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
   for (int li = 0; li < model->num_layers; ++li) {
@@ -493,7 +715,7 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
             cache->max_len, ws->q, ws->err, s, pdl);
     if (r != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, ws->attn,
-                  ws->attn_part, ws->attn_counters, ws->err, s, pdl);
+                  ws->attn_part, ws->attn_counters, ws->err, s, pdl, nullptr, 0, cache->cache_rows);
     if (r != QI_OK) return r;
     r = oproj(ws->attn, L.w_o, M, ws->x, ws->err, s, pdl);
     if (r != QI_OK) return r;

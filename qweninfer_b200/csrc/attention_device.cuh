@@ -1,0 +1,290 @@
+// One attention work unit — (key split, KV head, query token) — as a device function shared
+// by the standalone attention kernel (attention.cu) and the persistent forward
+// (forward_persistent.cu). 128 threads (4 warps) run a unit; `sync` is the whole CTA in
+// the standalone kernel and a named barrier of the four epilogue warps in the persistent
+// one. The two K/V stage mbarriers are initialised once per CTA; `uses` carries their
+// phase counts from unit to unit.
+#pragma once
+
+#include "common.cuh"
+#include "internal.h"
+#include "tc_proj.h"
+
+namespace qi {
+namespace attn {
+
+constexpr int kAttnThreads = 128;
+constexpr int kTile = 128;  // keys per stage
+constexpr int kPartStride = kGqa * (kHeadDim + 2);  // floats per (token, head, split) partial
+static_assert(2 * kGqa * kMaxAttnSplits + kGqa <= 4 * kGqa * (kHeadDim + 2), "split merge scratch");
+
+struct AttnSmem {
+  uint16_t k[2][kTile * kHeadDim];
+  uint16_t v[2][kTile * kHeadDim];
+  float q[kGqa * 2 * 8 * 4];          // per head: [half][chunk][4], scaled by 1/sqrt(64)
+  float p[4][32][8];                  // per warp: probabilities of its 32 keys, 7 heads
+  float cmb[4][kGqa][kHeadDim + 2];   // per warp: acc[64], m, l
+  uint64_t bar[2];
+  int last;
+};
+
+// Output element (token, feature f = head * 64 + d): fp32 and/or the o projection's
+// activation tiles (hi/lo bf16 halves).
+__device__ __forceinline__ void emit(const AttnParams& p, int tok, int f, float v) {
+  if (p.out) p.out[(long long)tok * kHidden + f] = v;
+  if (p.out_act) {
+    const uint16_t hi = f32_to_bf16_rn(v);
+    p.out_act[act_offset(tok, f, 0, kHidden, p.out_nt)] = hi;
+    p.out_act[act_offset(tok, f, 1, kHidden, p.out_nt)] = f32_to_bf16_rn(v - bf16_to_f32(hi));
+  }
+}
+
+// Runs unit (split, g, tok); returns true when it wrote the final output of (tok, g)
+// (a single split, or the last split to arrive, which merges all of them).
+template <bool kNamedBarrier>
+__device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S, int split, int g, int tok,
+                                               int tid, uint32_t (&uses)[2]) {
+  auto sync = [] {
+    if constexpr (kNamedBarrier) asm volatile("bar.sync 1, 128;" ::: "memory");
+    else __syncthreads();
+  };
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int ps = p.pos[tok];
+  const int row = p.rows[tok];
+  if (ps < 0 || ps >= p.max_len || row < 0 || (p.cache_rows > 0 && row >= p.cache_rows)) {
+    // outside the cache: reported, nothing read or written; split 0 still counts the
+    // (token, head) as finished for callers that wait on completions
+    if (split == 0 && tid == 0) atomicExch(p.err, QI_ERR_INDEX);
+    return split == 0;
+  }
+  const int nkeys = ps + 1;
+  const int nsplit = (nkeys + p.split_keys - 1) / p.split_keys;
+  if (split >= nsplit) return false;
+  const int kbeg = split * p.split_keys;
+  const int kend = min(nkeys, kbeg + p.split_keys);
+  const long long head_base = (((long long)row * kKvHeads + g) * p.max_len) * kHeadDim;
+  const uint16_t* kg = p.kc + head_base;
+  const uint16_t* vg = p.vc + head_base;
+
+  // q of the 7 heads sharing KV head g, pre-scaled by 1/8 (exact), laid out so that the
+  // eight 8-dim chunks' first halves are 16-byte neighbours (conflict-free rotated reads).
+  // (all four loads of a thread are issued before its shared-memory stores)
+  {
+    constexpr int kRounds = (kGqa * kHeadDim + kAttnThreads - 1) / kAttnThreads;
+    float qv[kRounds];
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int idx = tid + r * kAttnThreads;
+      qv[r] = __ldcg(p.q + (long long)tok * kHidden + g * kGqa * kHeadDim + (idx < kGqa * kHeadDim ? idx : 0));
+    }
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int idx = tid + r * kAttnThreads;
+      if (idx < kGqa * kHeadDim) {
+        const int h = idx >> 6, d = idx & 63;
+        const int cc = d >> 3, e = d & 7;
+        S.q[((h * 2 + (e >> 2)) * 8 + cc) * 4 + (e & 3)] = qv[r] * 0.125f;
+      }
+    }
+  }
+  sync();
+
+  const int ntiles = (kend - kbeg + kTile - 1) / kTile;
+  // mbarrier phases continue across the units a CTA runs: tile i uses stage i & 1
+  const uint32_t u0s = uses[0], u1s = uses[1];
+  uses[0] += (uint32_t)((ntiles + 1) >> 1);
+  uses[1] += (uint32_t)(ntiles >> 1);
+  auto parity = [&](int i) { return (uint32_t)((((i & 1) ? u1s : u0s) + (uint32_t)(i >> 1)) & 1u); };
+  auto issue = [&](int i) {
+    const int k0 = kbeg + i * kTile;
+    const int nk = min(kTile, kend - k0);
+    const uint32_t bytes = (uint32_t)nk * kHeadDim * 2;
+    const int st = i & 1;
+    mbar_arrive_expect_tx(&S.bar[st], 2 * bytes);
+    bulk_g2s(S.k[st], kg + (long long)k0 * kHeadDim, bytes, &S.bar[st]);
+    bulk_g2s(S.v[st], vg + (long long)k0 * kHeadDim, bytes, &S.bar[st]);
+  };
+  if (tid == 0) {
+    issue(0);
+    if (ntiles > 1) issue(1);
+  }
+
+  float m[kGqa], l[kGqa], acc[kGqa][2];
+#pragma unroll
+  for (int h = 0; h < kGqa; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+    acc[h][0] = acc[h][1] = 0.f;
+  }
+
+  for (int i = 0; i < ntiles; ++i) {
+    const int st = i & 1;
+    mbar_wait(&S.bar[st], parity(i), p.err);
+    const int k0 = kbeg + i * kTile;
+    const int nk = min(kTile, kend - k0);
+    const int kw = 32 * warp;
+    const int nkw = max(0, min(32, nk - kw));
+    if (nkw > 0) {
+      const bool valid = lane < nkw;
+      float s[kGqa];
+#pragma unroll
+      for (int h = 0; h < kGqa; ++h) s[h] = 0.f;
+      const uint16_t* krow = S.k[st] + (kw + lane) * kHeadDim;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int cc = (c + lane) & 7;
+        const uint4 kv = *reinterpret_cast<const uint4*>(krow + cc * 8);
+        const float k0f = bf16lo(kv.x), k1f = bf16hi(kv.x), k2f = bf16lo(kv.y), k3f = bf16hi(kv.y);
+        const float k4f = bf16lo(kv.z), k5f = bf16hi(kv.z), k6f = bf16lo(kv.w), k7f = bf16hi(kv.w);
+#pragma unroll
+        for (int h = 0; h < kGqa; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(&S.q[((h * 2 + 0) * 8 + cc) * 4]);
+          const float4 qb = *reinterpret_cast<const float4*>(&S.q[((h * 2 + 1) * 8 + cc) * 4]);
+          float a = s[h];
+          a = fmaf(qa.x, k0f, a);
+          a = fmaf(qa.y, k1f, a);
+          a = fmaf(qa.z, k2f, a);
+          a = fmaf(qa.w, k3f, a);
+          a = fmaf(qb.x, k4f, a);
+          a = fmaf(qb.y, k5f, a);
+          a = fmaf(qb.z, k6f, a);
+          a = fmaf(qb.w, k7f, a);
+          s[h] = a;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < kGqa; ++h) {
+        const float sv = valid ? s[h] : -INFINITY;
+        const float mn = fmaxf(m[h], warp_max(sv));
+        const float alpha = expf(m[h] - mn);
+        const float pr = valid ? expf(sv - mn) : 0.f;
+        l[h] = l[h] * alpha + warp_sum(pr);
+        acc[h][0] *= alpha;
+        acc[h][1] *= alpha;
+        m[h] = mn;
+        S.p[warp][lane][h] = pr;
+      }
+      __syncwarp();
+      const uint16_t* vt = S.v[st] + kw * kHeadDim + 2 * lane;
+      for (int j = 0; j < nkw; ++j) {
+        const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vt + j * kHeadDim);
+        const float v0 = bf16lo(v2), v1 = bf16hi(v2);
+        const float4 pa = *reinterpret_cast<const float4*>(&S.p[warp][j][0]);
+        const float4 pb = *reinterpret_cast<const float4*>(&S.p[warp][j][4]);
+        acc[0][0] = fmaf(pa.x, v0, acc[0][0]); acc[0][1] = fmaf(pa.x, v1, acc[0][1]);
+        acc[1][0] = fmaf(pa.y, v0, acc[1][0]); acc[1][1] = fmaf(pa.y, v1, acc[1][1]);
+        acc[2][0] = fmaf(pa.z, v0, acc[2][0]); acc[2][1] = fmaf(pa.z, v1, acc[2][1]);
+        acc[3][0] = fmaf(pa.w, v0, acc[3][0]); acc[3][1] = fmaf(pa.w, v1, acc[3][1]);
+        acc[4][0] = fmaf(pb.x, v0, acc[4][0]); acc[4][1] = fmaf(pb.x, v1, acc[4][1]);
+        acc[5][0] = fmaf(pb.y, v0, acc[5][0]); acc[5][1] = fmaf(pb.y, v1, acc[5][1]);
+        acc[6][0] = fmaf(pb.z, v0, acc[6][0]); acc[6][1] = fmaf(pb.z, v1, acc[6][1]);
+      }
+      __syncwarp();
+    }
+    sync();  // stage st fully consumed
+    if (tid == 0 && i + 2 < ntiles) issue(i + 2);
+  }
+
+  // Merge the 4 warps.
+#pragma unroll
+  for (int h = 0; h < kGqa; ++h) {
+    S.cmb[warp][h][2 * lane] = acc[h][0];
+    S.cmb[warp][h][2 * lane + 1] = acc[h][1];
+    if (lane == 0) {
+      S.cmb[warp][h][kHeadDim] = m[h];
+      S.cmb[warp][h][kHeadDim + 1] = l[h];
+    }
+  }
+  sync();
+  float* part = p.part + (((long long)tok * kKvHeads + g) * p.max_splits + split) * kPartStride;
+  for (int idx = tid; idx < kGqa * (kHeadDim + 2); idx += kAttnThreads) {
+    const int h = idx / (kHeadDim + 2);
+    const int d = idx - h * (kHeadDim + 2);
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, S.cmb[w][h][kHeadDim]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = S.cmb[w][h][kHeadDim];
+      if (mw == -INFINITY) continue;
+      const float sc = expf(mw - mx);
+      L = fmaf(sc, S.cmb[w][h][kHeadDim + 1], L);
+      if (d < kHeadDim) A = fmaf(sc, S.cmb[w][h][d], A);
+    }
+    if (nsplit == 1) {
+      if (d < kHeadDim) emit(p, tok, (g * kGqa + h) * kHeadDim + d, A / L);
+    } else {
+      part[idx] = d < kHeadDim ? A : (d == kHeadDim ? mx : L);
+    }
+  }
+  if (nsplit == 1) return true;
+
+  // Split merge by the last-arriving CTA of this (token, head). Release: the barrier
+  // orders every thread's partial stores before thread 0's fence and arrival.
+  sync();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned int prev = atomicAdd(&p.counters[tok * kKvHeads + g], 1u);
+    const bool last = prev == (unsigned int)(nsplit - 1);
+    if (last) __threadfence();
+    S.last = last;
+  }
+  sync();
+  if (!S.last) return false;
+  const float* base = p.part + (((long long)tok * kKvHeads + g) * p.max_splits) * kPartStride;
+  // (1) every split's running max and sum into shared memory (reusing the warp-merge
+  // area: 2 * 7 * nsplit + 7 floats), (2) per head the max and the split weights
+  // exp(m_s - max), (3) the weighted sum of the split outputs, loads before stores.
+  float* sm = &S.cmb[0][0][0];
+  for (int idx = tid; idx < kGqa * nsplit; idx += kAttnThreads) {
+    const int h = idx / nsplit, s = idx - h * nsplit;
+    const float* ph = base + s * kPartStride + h * (kHeadDim + 2);
+    const float mv = __ldcg(ph + kHeadDim), lv = __ldcg(ph + kHeadDim + 1);
+    sm[idx] = mv;
+    sm[kGqa * nsplit + idx] = lv;
+  }
+  sync();
+  if (tid < kGqa) {
+    const int h = tid;
+    float mx = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, sm[h * nsplit + s]);
+    float L = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float sc = expf(sm[h * nsplit + s] - mx);
+      L = fmaf(sc, sm[kGqa * nsplit + h * nsplit + s], L);
+      sm[h * nsplit + s] = sc;
+    }
+    sm[2 * kGqa * nsplit + h] = L;
+  }
+  sync();
+  {
+    constexpr int kRounds = (kGqa * kHeadDim + kAttnThreads - 1) / kAttnThreads;
+    float A[kRounds];
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) A[r] = 0.f;
+#pragma unroll 4
+    for (int s = 0; s < nsplit; ++s) {
+      const float* ps = base + s * kPartStride;
+#pragma unroll
+      for (int r = 0; r < kRounds; ++r) {
+        const int idx = tid + r * kAttnThreads;
+        if (idx < kGqa * kHeadDim) {
+          const int h = idx >> 6, d = idx & 63;
+          A[r] = fmaf(sm[h * nsplit + s], __ldcg(ps + h * (kHeadDim + 2) + d), A[r]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int idx = tid + r * kAttnThreads;
+      if (idx < kGqa * kHeadDim) emit(p, tok, g * kGqa * kHeadDim + idx, A[r] / sm[2 * kGqa * nsplit + (idx >> 6)]);
+    }
+  }
+  if (tid == 0) p.counters[tok * kKvHeads + g] = 0u;
+  return true;
+}
+
+}  // namespace attn
+}  // namespace qi

@@ -6,6 +6,9 @@
 
 namespace qi {
 
+// Key splits per query token that the attention split merge supports.
+constexpr int kMaxAttnSplits = 128;
+
 enum GemvEpilogue : int {
   kEpiQkvRope = 0,   // bias + RoPE; q -> fp32 buffer, k/v -> bf16 cache
   kEpiResidual = 1,  // out[t, n] += value
@@ -59,6 +62,7 @@ struct AttnParams {
   const int32_t* rows;
   int M;
   int max_len;
+  int cache_rows;  // rows of the cache (0: rows are not checked)
   int split_keys;
   int max_splits;
   float* out;         // fp32 (M, 896), may be null
@@ -71,10 +75,12 @@ struct AttnParams {
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
 
-// norm_w/NT/act/ss (optional, all or none): also emit activation tiles of norm_w * x and
-// per-token sums of squares for the tensor-core projections (tc_proj.h).
+// slots (optional): the first n_slots argmax slots are zeroed. norm_w/NT/act/ss (optional,
+// all or none): also emit activation tiles of norm_w * x and per-token sums of squares for
+// the tensor-core projections (tc_proj.h).
 cudaError_t launch_embed(const uint16_t* embed, int vocab, const int32_t* ids, int M, float* x,
-                         unsigned long long* slots, cudaStream_t stream, bool pdl, const float* norm_w = nullptr,
+                         unsigned long long* slots, int n_slots, cudaStream_t stream, bool pdl,
+                         const float* norm_w = nullptr,
                          int NT = 0, uint16_t* act = nullptr, float* ss = nullptr, int ss_ld = 0);
 
 cudaError_t launch_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_rows, int max_len,

@@ -13,7 +13,7 @@ namespace {
 // norm_w * x and the token's sum of squares into ss[0][t] (ss[1..6][t] = 0).
 __global__ void __launch_bounds__(128) embed_kernel(const uint16_t* __restrict__ embed, int vocab,
                                                      const int32_t* __restrict__ ids, int M, float* __restrict__ x,
-                                                     unsigned long long* __restrict__ slots,
+                                                     unsigned long long* __restrict__ slots, int n_slots,
                                                      const float* __restrict__ norm_w, int NT,
                                                      uint16_t* __restrict__ act, float* __restrict__ ss, int ss_ld) {
   __shared__ float red[4];
@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(128) embed_kernel(const uint16_t* __restrict__
       *reinterpret_cast<uint4*>(act + act_offset(t, k, 1, kHidden, NT)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
   }
-  if (slots && threadIdx.x == 0) slots[t] = 0ull;
+  if (slots && threadIdx.x == 0 && t < n_slots) slots[t] = 0ull;
   if (act && ss) {
     sq = warp_sum(sq);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
@@ -81,8 +81,8 @@ __global__ void __launch_bounds__(256) move_rows_kernel(uint16_t* __restrict__ k
 }  // namespace
 
 cudaError_t launch_embed(const uint16_t* embed, int vocab, const int32_t* ids, int M, float* x,
-                         unsigned long long* slots, cudaStream_t stream, bool pdl, const float* norm_w, int NT,
-                         uint16_t* act, float* ss, int ss_ld) {
+                         unsigned long long* slots, int n_slots, cudaStream_t stream, bool pdl,
+                         const float* norm_w, int NT, uint16_t* act, float* ss, int ss_ld) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M, 1, 1);
   cfg.blockDim = dim3(128, 1, 1);
@@ -92,7 +92,8 @@ cudaError_t launch_embed(const uint16_t* embed, int vocab, const int32_t* ids, i
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, embed_kernel, embed, vocab, ids, M, x, slots, norm_w, NT, act, ss, ss_ld);
+  return cudaLaunchKernelEx(&cfg, embed_kernel, embed, vocab, ids, M, x, slots, n_slots, norm_w, NT, act, ss,
+                            ss_ld);
 }
 
 cudaError_t launch_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_rows, int max_len,

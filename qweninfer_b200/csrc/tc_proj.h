@@ -53,6 +53,7 @@ struct TcParams {
   uint16_t* kc;
   uint16_t* vc;
   int max_len;
+  int cache_rows;  // rows of the cache (0: rows are not checked)
   // residual / swiglu
   float* x;
   const float* next_norm_w;

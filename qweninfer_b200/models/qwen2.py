@@ -266,6 +266,7 @@ def _split_plan(max_tokens: int, max_len: int) -> tuple[int, int]:
     """Key-split size and count for attention over `max_len` cache slots: fine splits
     (128 keys) when few queries must fill 148 SMs, coarse (1024) for prefill-sized M."""
     split = 128 if max_tokens <= 64 else 1024
+    split = max(split, -(-max_len // (128 * 128)) * 128)  # at most 128 splits (the merge's capacity)
     return split, max(1, -(-max_len // split))
 
 
@@ -286,6 +287,47 @@ def token_tile(M: int) -> int:
     while nt < M and nt < 128:
         nt *= 2
     return nt
+
+
+def use_persistent(M: int) -> bool:
+    """Whole forward as one cooperative launch for M <= 128 tokens on the tensor-core
+    path (QI_PERSISTENT=1). Off by default: its per-stage dependency chain is the same as
+    that of the per-stage launches, which measure faster."""
+    import os
+    return M <= 128 and use_tensor_cores() and os.environ.get("QI_PERSISTENT", "0") == "1"
+
+
+class PersistentPlan:
+    """Device copy of a persistent-forward stage table (qi_persistent_plan) for fixed
+    buffers; launch() enqueues the single cooperative kernel on the current stream.
+    Planning is done once per buffer configuration: it fills a pinned host buffer
+    (`host`, shared by the caller's plans), copies it to the device and waits for the copy."""
+
+    TABLE_BYTES = 256 * 1024
+
+    @staticmethod
+    def host_buffer() -> torch.Tensor:
+        return torch.empty(PersistentPlan.TABLE_BYTES, dtype=torch.uint8, pin_memory=True)
+
+    def __init__(self, model, cache, ws, ids_ptr, pos_ptr, rows_ptr, M, head_lo, head_stride, n_head,
+                 logits_ptr, logits_bf16, logits_ld, slots_ptr, host: torch.Tensor) -> None:
+        n = C.c_int(0)
+        L = _lib.lib()
+        _lib.check(L.qi_persistent_plan(
+            C.byref(model.native()), C.byref(cache.native()), C.byref(ws.struct), ids_ptr, pos_ptr, rows_ptr, M,
+            head_lo, head_stride, n_head, logits_ptr, logits_bf16, logits_ld, slots_ptr, host.data_ptr(),
+            host.numel(), C.byref(n)), "qi_persistent_plan")
+        self.n_stages = n.value
+        used = self.n_stages * L.qi_persistent_stage_bytes()
+        self.table = torch.empty(used, dtype=torch.uint8, device=model.device)
+        self.table.copy_(host[:used], non_blocking=True)
+        torch.cuda.current_stream(model.device).synchronize()  # `host` may be refilled next
+        self.ws, self.M, self.dev = ws, M, model.device
+        self._keep = (model, cache)  # the table points into their tensors
+
+    def launch(self) -> None:
+        _lib.check(_lib.lib().qi_persistent_launch(self.table.data_ptr(), self.n_stages, C.byref(self.ws.struct),
+                                                   self.M, _lib.stream_ptr(self.dev)), "qi_persistent_launch")
 
 
 def use_tensor_cores() -> bool:
@@ -324,12 +366,15 @@ class Workspace:
         self.tc_scratch = torch.empty(sms * 2 * 128 * nt, **f32)
         n_counters = max(76 * (pad // nt), -(-vocab // 128), 64)
         self.tc_counters = torch.zeros(n_counters, dtype=torch.int32, device=device)
+        self.persist_done = torch.zeros(512 * 32, dtype=torch.int32, device=device)  # 512 stages, 128 B apart
+        self.persist_trace = torch.zeros(513, dtype=torch.int64, device=device)
         self.struct = _lib.QiWorkspace(
             self.x.data_ptr(), self.q.data_ptr(), self.attn.data_ptr(), self.h.data_ptr(),
             self.attn_part.data_ptr(), self.attn_counters.data_ptr(), max_tokens, 1, 128, self.err.data_ptr(),
             int(use_tensor_cores()), self.act_x.data_ptr(), self.act_attn.data_ptr(), self.act_h.data_ptr(),
             self.ss.data_ptr(), pad, self.tc_scratch.data_ptr(), self.tc_scratch.numel(),
-            self.tc_counters.data_ptr(), n_counters)
+            self.tc_counters.data_ptr(), n_counters, self.persist_done.data_ptr(), self.persist_done.numel(),
+            self.persist_trace.data_ptr())
 
     def plan(self, M: int) -> "Workspace":
         self.struct.split_keys, self.struct.max_splits = _split_plan(M, self.max_len)
@@ -473,6 +518,15 @@ class Qwen2(nn.Module):
         logits = torch.empty(n_head, self.cfg.vocab_size, dtype=ldt, device=dev)
         slots = torch.zeros(M, dtype=torch.int64, device=dev)
         ws = self.workspace(max(M, 1), cache.max_len).plan(M)
+        if use_persistent(M):
+            if getattr(self, "_plan_host", None) is None:
+                self._plan_host = PersistentPlan.host_buffer()
+            plan = PersistentPlan(self, cache, ws, ids32.data_ptr(), pos32.data_ptr(), rows32.data_ptr(), M, head_lo,
+                                  head_stride, n_head, logits.data_ptr(), int(ldt == torch.bfloat16),
+                                  self.cfg.vocab_size, slots.data_ptr(), self._plan_host)
+            plan.launch()
+            self.last_argmax = self.decode_argmax(slots[:n_head])
+            return logits.view(B, 1 if last_only else S, self.cfg.vocab_size)
         _lib.check(_lib.lib().qi_forward(
             C.byref(self.native()), C.byref(cache.native()), C.byref(ws.struct), ids32.data_ptr(),
             pos32.data_ptr(), rows32.data_ptr(), M, head_lo, head_stride, n_head, logits.data_ptr(),
