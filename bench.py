@@ -15,9 +15,11 @@ Printed JSON (rank 0, one line):
   e2e    output tokens / time of Engine.run through the public API, CUDA events around
          the whole run: host bookkeeping, per-step H2D of (ids, positions, rows) from
          pinned memory and D2H of the argmax words included.
-  roofline  the gate/up+SwiGLU projection kernel (the largest per-layer weight stream)
-         at the trace's mean decode batch, timed alone over the 24 layers' distinct
-         weights (418 MB > L2), achieved HBM GB/s vs the measured copy peak.
+  roofline  the gate/up+SwiGLU tensor-core projection (tc_proj_kernel<swiglu>, the
+         largest per-layer weight stream) at the trace's mean decode batch, timed alone
+         over the 24 layers' distinct weights (418 MB > L2), achieved HBM GB/s vs the
+         measured copy peak; traffic = DRAM bytes per launch from an ncu capture
+         (profiles/tc_proj_swiglu_decode.md).
   cpu_baseline  the numpy oracle (the reference's algorithm restated) on the host cores
          over a bounded sample of the same workload.
 
@@ -48,6 +50,9 @@ sys.path.insert(0, str(REPO))
 MAX_LEN = 512
 WEIGHT_BYTES = 988_065_536          # bf16 layer weights + norms + biases + tied head
 KV_BYTES_PER_TOKEN = 12_288         # 2 (K,V) * 24 layers * 2 heads * 64 * 2 B
+# DRAM bytes (read + write) per launch of tc_proj_kernel<swiglu> by token tile, from one
+# ncu capture of the same launch (profiles/tc_proj_swiglu_decode.md); None until captured.
+TRAFFIC: dict[int, int | None] = {32: 18_066_944}
 EMBED_ROW_BYTES = 1_792
 
 
@@ -60,6 +65,9 @@ def parse():
     ap.add_argument("--slots", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=15.0)
+    ap.add_argument("--only", choices=["roofline"], default=None,
+                    help="roofline: only the timed gate/up projection loop (the profiling case)")
+    ap.add_argument("--batch", type=int, default=22, help="decode batch of --only roofline")
     return ap.parse_args()
 
 
@@ -272,39 +280,57 @@ def our_arm(args, rank: int, world: int, device: torch.device) -> dict | None:
 
 
 def kernel_roofline(model, M: int, pk: dict) -> dict:
-    """gate/up + SwiGLU projection at batch M over the 24 layers' distinct weights."""
+    """The forward's gate/up + SwiGLU projection (tc_proj_kernel<swiglu>, the launch
+    qi_forward issues for it, through qi_tc_gate_up_swiglu) at decode batch M, cycling
+    through the 24 layers' distinct weights (418 MB > L2), CUDA events on its stream."""
     import ctypes as C
     from qweninfer_b200 import _lib
+    from qweninfer_b200.models.qwen2 import token_tile
     dev = model.device
-    x = torch.randn(M, 896, device=dev)
-    h = torch.empty(M, 4864, device=dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    ln = [blk.post_attention_layernorm.weight.float().contiguous() for blk in model.layers]
+    NT = token_tile(M)
+    Mp = -(-M // NT) * NT
     L = _lib.lib()
     s = _lib.stream_ptr(dev)
+    x = torch.randn(M, 896, device=dev)
+    nw = model.layers[0].post_attention_layernorm.weight.float().contiguous()
+    act = torch.zeros(Mp * 896 * 2, dtype=torch.int16, device=dev)
+    ss = torch.zeros(7 * Mp, device=dev)
+    _lib.check(L.qi_act_tiles(x.data_ptr(), nw.data_ptr(), M, 896, NT, act.data_ptr(), ss.data_ptr(), Mp, s),
+               "act_tiles")
+    out = torch.zeros(Mp * 4864 * 2, dtype=torch.int16, device=dev)
+    scratch = torch.empty(148 * 2 * 128 * NT, device=dev)
+    counters = torch.zeros(1024, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws = [blk.mlp.w_gate_up_tiled.data_ptr() for blk in model.layers]
 
     def launch_all():
-        for li, blk in enumerate(model.layers):
-            _lib.check(L.qi_gate_up_swiglu(x.data_ptr(), ln[li].data_ptr(), C.c_float(1e-6),
-                                           blk.mlp.w_gate_up_tiled.data_ptr(), M, h.data_ptr(), err.data_ptr(), s),
-                       "gate_up")
+        for w in ws:
+            _lib.check(L.qi_tc_gate_up_swiglu(w, act.data_ptr(), M, NT, ss.data_ptr(), Mp, C.c_float(1e-6),
+                                              out.data_ptr(), scratch.data_ptr(), scratch.numel(),
+                                              counters.data_ptr(), counters.numel(), 0, err.data_ptr(), s),
+                       "tc_gate_up_swiglu")
 
     for _ in range(3):
         launch_all()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 10
+    reps = 20
     a.record()
     for _ in range(reps):
         launch_all()
     b.record()
     b.synchronize()
-    per_launch_s = a.elapsed_time(b) / 1e3 / (reps * len(model.layers))
-    algo = 9728 * 896 * 2 + M * 896 * 4 + M * 4864 * 4
+    if int(err.item()) != 0:
+        raise RuntimeError("gate/up kernel reported an error")
+    per_launch_s = a.elapsed_time(b) / 1e3 / (reps * len(ws))
+    # algorithmic bytes: weights once, activation tiles in (hi/lo bf16), the 7 partial sums
+    # of squares, SwiGLU activation tiles out (hi/lo bf16), for the M live tokens
+    algo = 9728 * 896 * 2 + M * 896 * 4 + 7 * M * 4 + M * 4864 * 4
     gbs = algo / per_launch_s / 1e9
-    return {"kernel": "gemv_kernel<swiglu> (RMSNorm + gate/up projection + SwiGLU)", "bound": "hbm",
+    return {"kernel": "tc_proj_kernel<swiglu>: RMSNorm-folded gate/up projection + SwiGLU (tcgen05, stream-K, "
+                      "148 CTAs), the forward's largest weight stream", "bound": "hbm",
             "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"],
-            "peak_source": pk["source"], "traffic": None, "batch": M, "us_per_launch": per_launch_s * 1e6,
-            "algorithmic_bytes_per_launch": algo}
+            "peak_source": pk["source"], "traffic": TRAFFIC.get(NT), "batch": M, "token_tile": NT,
+            "us_per_launch": per_launch_s * 1e6, "algorithmic_bytes_per_launch": algo}
 
 
 def batch1_latency(model) -> dict:
@@ -392,6 +418,9 @@ def main() -> None:
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.only == "roofline":
+        print(json.dumps(kernel_roofline(load_model(device), args.batch, peaks())), flush=True)
+        return
     if world > 1:
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     try:

@@ -76,6 +76,7 @@ SIGNATURES = {
     "qi_persistent_launch": (i32, [vp, i32, C.POINTER(QiWorkspace), i32, vp]),
     "qi_act_tiles": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp]),
     "qi_tc_linear": (i32, [vp, i32, i32, vp, i32, i32, vp, i32, f32, vp, i32, vp, i64, vp, i32, i32, vp, vp]),
+    "qi_tc_gate_up_swiglu": (i32, [vp, vp, i32, i32, vp, i32, f32, vp, vp, i64, vp, i32, i32, vp, vp]),
 }
 
 _lock = threading.Lock()

@@ -690,6 +690,29 @@ int qi_tc_linear(const uint16_t* w, int n_rows, int K, const uint16_t* act, int 
   return run_tc(p, scratch, scratch_floats, counters, counters_len, ctas, as_stream(stream), false);
 }
 
+int qi_tc_gate_up_swiglu(const uint16_t* w_gate_up, const uint16_t* act, int M, int NT, const float* ss, int ss_ld,
+                         float eps, uint16_t* act_out, float* scratch, long long scratch_floats,
+                         unsigned int* counters, int counters_len, int ctas, int* err, qi_stream_t stream) {
+  if (M <= 0 || bad_nt(NT) || bad_ptr(w_gate_up) || bad_ptr(act) || bad_ptr(act_out) || bad_ptr(scratch) ||
+      bad_ptr(counters) || (ss && ss_ld < round_up(M, NT)))
+    return QI_ERR_ARG;
+  TcParams p = {};
+  p.w = w_gate_up;
+  p.KB = kHidden / 64;
+  p.n_mtiles = kGateUpRows / 128;
+  p.act_in = act;
+  p.NT = NT;
+  p.n_ntiles = (M + NT - 1) / NT;
+  p.M = M;
+  p.ss_in = ss;
+  p.ss_ld = ss_ld;
+  p.eps = eps;
+  p.epi = kTcSwiglu;
+  p.act_out = act_out;
+  p.err = err;
+  return run_tc(p, scratch, scratch_floats, counters, counters_len, ctas, as_stream(stream), false);
+}
+
 int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
                const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
                void* logits, int logits_bf16, long long logits_ld, unsigned long long* argmax_slots,

@@ -189,3 +189,49 @@ def test_tc_linear_batch_invariant():
     for M in (1, 5, 22):
         part = _tc_linear(w, x[:M])
         assert np.array_equal(part, full[:M]), M
+
+
+def decode_act_tiles(act: np.ndarray, M: int, K: int, NT: int) -> np.ndarray:
+    """hi + lo of activation tiles (uint16 bf16 bit patterns) as fp32 (M, K)."""
+    t, k = np.meshgrid(np.arange(M), np.arange(K), indexing="ij")
+    hi = (act[act_offset(t, k, 0, K, NT)].astype(np.uint32) << 16).view(np.float32)
+    lo = (act[act_offset(t, k, 1, K, NT)].astype(np.uint32) << 16).view(np.float32)
+    return hi + lo
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 22, 100])
+def test_tc_gate_up_swiglu_matches_fp64(M):
+    """qi_tc_gate_up_swiglu (the forward's gate/up launch): RMSNorm folded, interleaved
+    gate/up rows, SwiGLU, activation tiles for the down projection."""
+    _lib.ensure_device(torch.device(DEV, 0))
+    rng = np.random.default_rng(40 + M)
+    wg = bf16_round(rng.normal(0, 0.02, (4864, 896)).astype(np.float32))
+    wu = bf16_round(rng.normal(0, 0.02, (4864, 896)).astype(np.float32))
+    w = np.empty((9728, 896), np.float32)  # the fused layout: gate row 2i, up row 2i+1
+    w[0::2], w[1::2] = wg, wu
+    nw = bf16_round((1 + 0.1 * rng.standard_normal(896)).astype(np.float32))
+    x = (2 * rng.standard_normal((M, 896))).astype(np.float32)
+    NT = token_tile(M)
+    Mp = -(-M // NT) * NT
+    L = _lib.lib()
+    s = _lib.stream_ptr()
+    act = dev(torch.zeros(Mp * 896 * 2, dtype=torch.int16))
+    ss = dev(torch.zeros(7 * Mp))
+    _lib.check(L.qi_act_tiles(dev(torch.from_numpy(x)).data_ptr(), dev(torch.from_numpy(nw)).data_ptr(), M, 896, NT,
+                              act.data_ptr(), ss.data_ptr(), Mp, s), "act_tiles")
+    wt = dev(tile_weight(torch.from_numpy(w).to(torch.bfloat16)))
+    out = dev(torch.zeros(Mp * 4864 * 2, dtype=torch.int16))
+    scratch = dev(torch.empty(148 * 2 * 128 * NT))
+    counters = dev(torch.zeros(4096, dtype=torch.int32))
+    err = dev(torch.zeros(1, dtype=torch.int32))
+    _lib.check(L.qi_tc_gate_up_swiglu(wt.data_ptr(), act.data_ptr(), M, NT, ss.data_ptr(), Mp, C.c_float(1e-6),
+                                      out.data_ptr(), scratch.data_ptr(), scratch.numel(), counters.data_ptr(), 4096,
+                                      0, err.data_ptr(), s), "tc_gate_up_swiglu")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0 and int(counters.abs().sum()) == 0
+    got = decode_act_tiles(out.cpu().numpy().view(np.uint16), M, 4864, NT)
+    xn = rmsnorm(x, nw, 1e-6).astype(np.float64)
+    g, u = xn @ wg.T.astype(np.float64), xn @ wu.T.astype(np.float64)
+    ref = g / (1 + np.exp(-g)) * u
+    assert np.abs(got - ref).max() / np.abs(ref).max() < 2e-5
