@@ -112,7 +112,8 @@ def check(code: int, what: str) -> None:
     if code != QI_OK:
         names = {QI_ERR_ARG: "invalid argument", QI_ERR_TIMEOUT: "device wait timed out",
                  QI_ERR_DEVICE: "not an sm_100 (B200) device",
-                 QI_ERR_TOO_LARGE: "size beyond the entry point's fixed capacity"}
+                 QI_ERR_TOO_LARGE: "size beyond the entry point's fixed capacity",
+                 QI_ERR_INDEX: "a position or cache row outside the cache"}
         raise QiError(f"{what} failed: {names.get(code, f'CUDA error {code}')}")
 
 

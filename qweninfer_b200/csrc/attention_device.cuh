@@ -221,16 +221,10 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   }
   if (nsplit == 1) return true;
 
-  // Split merge by the last-arriving CTA of this (token, head). Release: the barrier
-  // orders every thread's partial stores before thread 0's fence and arrival.
+  // Split merge by the last-arriving CTA of this (token, head): the barrier orders every
+  // thread's partial stores before thread 0's acq_rel arrival.
   sync();
-  if (tid == 0) {
-    __threadfence();
-    const unsigned int prev = atomicAdd(&p.counters[tok * kKvHeads + g], 1u);
-    const bool last = prev == (unsigned int)(nsplit - 1);
-    if (last) __threadfence();
-    S.last = last;
-  }
+  if (tid == 0) S.last = atomic_add_acq_rel(&p.counters[tok * kKvHeads + g], 1u) == (unsigned int)(nsplit - 1);
   sync();
   if (!S.last) return false;
   const float* base = p.part + (((long long)tok * kKvHeads + g) * p.max_splits) * kPartStride;

@@ -90,8 +90,7 @@ __device__ __forceinline__ void signal_done(const Done& d, int et) {
   fence_proxy_async_global();  // consumers read these writes with bulk copies
   epi_bar();
   if (et == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(d.ctr, 1u);
+    const unsigned prev = atomic_add_acq_rel(d.ctr, 1u);
     if (d.stamp && prev + 1 == d.target) *d.stamp = global_timer_ns();
   }
 }

@@ -79,35 +79,6 @@ struct Geom {
 
 // ------------------------------------------------------------------ epilogues
 
-// Address of (token t, column k) in activation tiles, split into a per-thread part (the
-// column this thread writes) and a per-token part; NT is a power of two.
-struct ActAddr {
-  long long col;         // k-dependent offset (hi half)
-  long long half;        // offset of the lo half
-  long long ntile;       // elements per token tile
-  int lg;
-  __device__ __forceinline__ long long tok(int t) const {
-    const int tl = t & ((1 << lg) - 1);
-    return (long long)(t >> lg) * ntile + (tl >> 3) * 512 + (tl & 7) * 8;
-  }
-};
-
-__device__ __forceinline__ ActAddr act_addr(int k, int K, int NT, int lg) {
-  ActAddr a;
-  a.col = (long long)(k >> 6) * (2LL * NT * 64) + ((k & 63) >> 3) * 64 + (k & 7);
-  a.half = (long long)NT * 64;
-  a.ntile = (long long)(K / 64) * 2LL * NT * 64;
-  a.lg = lg;
-  return a;
-}
-
-__device__ __forceinline__ void act_store(uint16_t* act, const ActAddr& a, int t, float v) {
-  const uint16_t hi = f32_to_bf16_rn(v);
-  const long long o = a.tok(t) + a.col;
-  act[o] = hi;
-  act[o + a.half] = f32_to_bf16_rn(v - bf16_to_f32(hi));
-}
-
 // Shared-memory scratch of the four epilogue warps (carve_epi lays it out).
 struct EpiSmem {
   unsigned long long* abest;  // 128 packed argmax candidates of the token tile
@@ -116,8 +87,9 @@ struct EpiSmem {
   int* tpos;                  // 128 positions of the current token tile
   int* trow;                  // 128 cache rows of the current token tile
   int* flag;                  // last-contributor broadcast
+  uint16_t* stage;            // 4 x 1024: per-warp staging of activation-tile stores
 };
-constexpr size_t kEpiSmemBytes = 128 * 8 + 64 * 4 + 128 * 4 + 128 * 4 + 128 * 4 + 16;
+constexpr size_t kEpiSmemBytes = 128 * 8 + 64 * 4 + 128 * 4 + 128 * 4 + 128 * 4 + 16 + 4 * 1024 * 2;
 
 __device__ __forceinline__ EpiSmem carve_epi(uint8_t* base) {  // base 8-byte aligned
   EpiSmem e;
@@ -127,7 +99,47 @@ __device__ __forceinline__ EpiSmem carve_epi(uint8_t* base) {  // base 8-byte al
   e.tpos = reinterpret_cast<int*>(e.rsm + 128);
   e.trow = e.tpos + 128;
   e.flag = e.trow + 128;
+  e.stage = reinterpret_cast<uint16_t*>(base + 2832);  // 16-byte aligned when base is
   return e;
+}
+
+// Activation-tile store of one warp for the CT tokens tbase.. of a chunk: lane L holds
+// val[i] for column k0 + (L >> SHIFT) (SHIFT 1: the even lanes hold 16 columns; SHIFT 0:
+// all lanes, 32 columns; the columns lie in one 64-column block). The hi/lo halves go to
+// the warp's staging buffer in the tile layout, then out as 16-byte rows of core matrices
+// (2-4 vector stores per lane instead of 2 * CT scattered 2-byte stores). Live tokens only.
+template <int CT, int SHIFT>
+__device__ __forceinline__ void act_store_warp(uint16_t* act, int K, int NT, int lg, int k0, int tbase, int nlive,
+                                               const float (&val)[CT], uint16_t* wbuf, int lane) {
+  constexpr int KG = (32 >> SHIFT) / 8;  // 8-column groups of the warp
+  constexpr int TG = CT / 8;             // 8-token groups of the chunk
+  if ((lane & ((1 << SHIFT) - 1)) == 0) {
+    const int col = lane >> SHIFT, kg = col >> 3, kk = col & 7;
+#pragma unroll
+    for (int i = 0; i < CT; ++i) {
+      const uint16_t hi = f32_to_bf16_rn(val[i]);
+      const uint16_t lo = f32_to_bf16_rn(val[i] - bf16_to_f32(hi));
+      wbuf[((0 * TG + (i >> 3)) * KG + kg) * 64 + (i & 7) * 8 + kk] = hi;
+      wbuf[((1 * TG + (i >> 3)) * KG + kg) * 64 + (i & 7) * 8 + kk] = lo;
+    }
+  }
+  __syncwarp();
+  const long long kpart = (long long)(k0 >> 6) * (2LL * NT * 64) + ((k0 & 63) >> 3) * 64;
+  const long long ntile = (long long)(K / 64) * 2LL * NT * 64;
+#pragma unroll
+  for (int r = 0; r < (2 * TG * KG * 8) / 32; ++r) {
+    const int v = lane + 32 * r;
+    const int t = v & 7, kg = (v >> 3) % KG, tg = ((v >> 3) / KG) % TG, part = (v >> 3) / (KG * TG);
+    const int i = tg * 8 + t;
+    if (i < nlive) {
+      const int tok = tbase + i, tl = tok & ((1 << lg) - 1);
+      const long long o = (long long)(tok >> lg) * ntile + kpart + (long long)part * NT * 64 + (tl >> 3) * 512 +
+                          kg * 64 + (tl & 7) * 8;
+      *reinterpret_cast<uint4*>(act + o) =
+          *reinterpret_cast<const uint4*>(wbuf + ((part * TG + tg) * KG + kg) * 64 + t * 8);
+    }
+  }
+  __syncwarp();
 }
 
 // Final epilogue of weight row n (this thread) for tokens tbase .. tbase+nlive-1 (the
@@ -139,7 +151,7 @@ __device__ __forceinline__ EpiSmem carve_epi(uint8_t* base) {  // base 8-byte al
 template <int EPI, int CT>
 __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase, int nlive, const float (&v)[CT],
                                             const float* rs, const int* tpos, const int* trow, int lane, int ew,
-                                            float* sred, unsigned long long* abest) {
+                                            float* sred, unsigned long long* abest, uint16_t* wbuf) {
   if constexpr (EPI == kTcPlain) {
 #pragma unroll
     for (int i = 0; i < CT; ++i)
@@ -181,32 +193,35 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
     }
   } else if constexpr (EPI == kTcSwiglu) {
     // silu(gate) * up (qwen2.py:114-116); gate row 2i, up row 2i+1
-    const ActAddr a = act_addr(n >> 1, kInter, p.NT, p.lg_nt);
+    float h[CT];
 #pragma unroll
     for (int i = 0; i < CT; ++i) {
-      if (i >= nlive) break;
       const float x = v[i] * rs[i];
       const float up = __shfl_xor_sync(0xffffffffu, x, 1);
-      if (!(n & 1)) act_store(p.act_out, a, tbase + i, x / (1.0f + expf(-x)) * up);
+      h[i] = __fdividef(x, 1.0f + __expf(-x)) * up;
     }
+    act_store_warp<CT, 1>(p.act_out, kInter, p.NT, p.lg_nt, (n - lane) >> 1, tbase, nlive, h, wbuf, lane);
   } else if constexpr (EPI == kTcResidual) {
     // residual add into the fp32 stream (qwen2.py:237-239), then the next projection's
     // activations hi/lo(w_next * x) and this tile's partial sums of squares of x
     const float wn = p.next_norm_w ? __ldg(p.next_norm_w + n) : 1.0f;
-    const ActAddr a = act_addr(n, kHidden, p.NT, p.lg_nt);
-    float xo[CT];
+    float xo[CT], an[CT];
 #pragma unroll
-    for (int i = 0; i < CT; ++i) xo[i] = __ldcg(p.x + (long long)(tbase + (i < nlive ? i : 0)) * kHidden + n);
+    for (int i = 0; i < CT; ++i) {
+      xo[i] = __ldcg(p.x + (long long)(tbase + (i < nlive ? i : 0)) * kHidden + n);
+      an[i] = 0.f;
+    }
 #pragma unroll
     for (int i = 0; i < CT; ++i) {
       if (i >= nlive) break;
       const int t = tbase + i;
       const float xv = xo[i] + v[i];
       p.x[(long long)t * kHidden + n] = xv;
-      if (p.act_out) act_store(p.act_out, a, t, xv * wn);
+      an[i] = xv * wn;
       const float s = warp_sum(xv * xv);
       if (lane == 0) sred[ew * 16 + i] = s;
     }
+    if (p.act_out) act_store_warp<CT, 0>(p.act_out, kHidden, p.NT, p.lg_nt, n - lane, tbase, nlive, an, wbuf, lane);
     if (p.ss_out) {
       epi_bar();
       if (ew == 0 && lane < nlive)
@@ -290,103 +305,109 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
     mbar_wait(&acc_full[b], (uint32_t)((seg >> 1) & 1), p.err);
     tc_fence_after();
     const uint32_t t_base = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * N);
-    float* my_part = nullptr;
-    if (!whole) {
-      const int slot = (geo.start(cta) >= tile * p.KB) ? 0 : 1;
-      my_part = p.scratch + (((long long)cta * 2 + slot) * 128 + row) * NT;
-    }
-    for (int c = 0; c < NT && c < live; c += CT) {
-      float r[16], v[16];
+    const int nchunks = (min(NT, live) + CT - 1) / CT;
+    // accumulator chunk c (columns c*CT..) with its hi and lo halves summed
+    auto tmem_chunk = [&](int c, float (&v)[CT]) {
+      float r[16];
       if (NT == 8) {
         tmem_ld16(t_base, r);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = r[i] + r[8 + i];
+#pragma unroll
+        for (int i = 8; i < 16; ++i) v[i] = 0.f;
       } else {
         float lo[16];
-        tmem_ld16(t_base + (uint32_t)c, r);
-        tmem_ld16(t_base + (uint32_t)(NT + c), lo);
+        tmem_ld16(t_base + (uint32_t)(c * CT), r);
+        tmem_ld16(t_base + (uint32_t)(NT + c * CT), lo);
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] = r[i] + lo[i];
       }
-      const int nlive = min(min(CT, NT - c), live - c);
-      if (whole) {
-        finish_rows<EPI, CT>(p, n, tok0 + c, nlive, v, es.rsm + c, es.tpos + c, es.trow + c, lane, ew, es.sred,
-                             es.abest);
-      } else {
+    };
+    bool finish = whole;
+    int c_first = cta, c_last = cta;
+    if (!whole) {
+      // publish this CTA's partial sum of the tile, then arrive on the tile's counter
+      // (acq_rel: releases the partial stores of all 128 threads, ordered before it by the
+      // barrier, and acquires the other contributors' if this arrival is the last)
+      const int slot = (geo.start(cta) >= tile * p.KB) ? 0 : 1;
+      float* my_part = p.scratch + (((long long)cta * 2 + slot) * 128 + row) * NT;
+      for (int c = 0; c < nchunks; ++c) {
+        float v[CT];
+        tmem_chunk(c, v);
+        const int nlive = min(CT, live - c * CT);
         for (int i = 0; i < nlive; i += 4)
-          *reinterpret_cast<float4*>(my_part + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          *reinterpret_cast<float4*>(my_part + c * CT + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      c_first = geo.owner(tile * p.KB);
+      c_last = geo.owner(tile * p.KB + p.KB - 1);
+      epi_bar();
+      if (et == 0) *es.flag = atomic_add_acq_rel(&p.counters[tile], 1u) == (unsigned)(c_last - c_first);
+      epi_bar();
+      finish = *es.flag != 0;
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&acc_empty[b]);
-    if (whole) {
-      on_tile(et);
-    } else {
-      // arrive on the tile's counter (release: the barrier orders the 128 threads'
-      // partial stores before thread 0's fence); the last contributor acquires the others'
-      epi_bar();
-      const int c_first = geo.owner(tile * p.KB);
-      const int c_last = geo.owner(tile * p.KB + p.KB - 1);
-      if (et == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(&p.counters[tile], 1u);
-        const bool last = prev == (unsigned)(c_last - c_first);
-        if (last) __threadfence();
-        *es.flag = last;
-      }
-      epi_bar();
-      if (*es.flag) {
-        for (int c = 0; c < NT && c < live; c += CT) {
-          const int nlive = min(min(CT, NT - c), live - c);
-          float v[16];
+    if (finish) {
+      // The tile's final values, chunk by chunk: from TMEM (whole segment) or the sum of
+      // every contributor's partial in k order (deterministic whatever the arrival order).
+      // The partial loads of chunk c+1 are issued before chunk c's epilogue stores.
+      constexpr int kBatch = 4;
+      float4 q[kBatch][CT / 4];
+      auto issue = [&](int c, int cc0) {
+        const int nlive = min(CT, live - c * CT);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0.f;
-          // contributors are summed in k order; loads are issued 4 contributors ahead
-          auto src_of = [&](int cc) {
-            const int slot = (geo.start(cc) >= tile * p.KB) ? 0 : 1;
-            return p.scratch + (((long long)cc * 2 + slot) * 128 + row) * NT + c;
-          };
-          int cc = c_first;
-          for (; cc + 3 <= c_last; cc += 4) {
-            float4 q[4][4];
+        for (int a = 0; a < kBatch; ++a) {
+          const int cc = cc0 + a;
+          const bool on = cc <= c_last;
+          const int slot = (geo.start(on ? cc : c_first) >= tile * p.KB) ? 0 : 1;
+          const float* src = p.scratch + (((long long)(on ? cc : c_first) * 2 + slot) * 128 + row) * NT + c * CT;
 #pragma unroll
-            for (int a = 0; a < 4; ++a) {
-              const float* src = src_of(cc + a);
-#pragma unroll
-              for (int i4 = 0; i4 < 4; ++i4)
-                q[a][i4] = (4 * i4 < nlive) ? __ldcg(reinterpret_cast<const float4*>(src + 4 * i4))
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-              for (int i4 = 0; i4 < 4; ++i4) {
-                v[4 * i4] += q[a][i4].x;
-                v[4 * i4 + 1] += q[a][i4].y;
-                v[4 * i4 + 2] += q[a][i4].z;
-                v[4 * i4 + 3] += q[a][i4].w;
-              }
-          }
-          for (; cc <= c_last; ++cc) {
-            const float* src = src_of(cc);
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-              if (i < nlive) {
-                const float4 q4 = __ldcg(reinterpret_cast<const float4*>(src + i));
-                v[i] += q4.x;
-                v[i + 1] += q4.y;
-                v[i + 2] += q4.z;
-                v[i + 3] += q4.w;
-              }
-            }
-          }
-          finish_rows<EPI, CT>(p, n, tok0 + c, nlive, v, es.rsm + c, es.tpos + c, es.trow + c, lane, ew, es.sred,
-                               es.abest);
+          for (int i4 = 0; i4 < CT / 4; ++i4)
+            q[a][i4] = (on && 4 * i4 < nlive) ? __ldcg(reinterpret_cast<const float4*>(src + 4 * i4))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if (et == 0) p.counters[tile] = 0u;
-        on_tile(et);
+      };
+      auto reduce = [&](float (&v)[CT]) {
+#pragma unroll
+        for (int a = 0; a < kBatch; ++a)
+#pragma unroll
+          for (int i4 = 0; i4 < CT / 4; ++i4) {
+            v[4 * i4] += q[a][i4].x;
+            v[4 * i4 + 1] += q[a][i4].y;
+            v[4 * i4 + 2] += q[a][i4].z;
+            v[4 * i4 + 3] += q[a][i4].w;
+          }
+      };
+      if (!whole) issue(0, c_first);
+#pragma unroll 1
+      for (int c = 0; c < nchunks; ++c) {
+        float v[CT];
+        if (whole) {
+          tmem_chunk(c, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < CT; ++i) v[i] = 0.f;
+          for (int cc0 = c_first;;) {
+            reduce(v);
+            cc0 += kBatch;
+            if (cc0 <= c_last) issue(c, cc0);
+            else break;
+          }
+          if (c + 1 < nchunks) issue(c + 1, c_first);
+        }
+        const int nlive = min(CT, live - c * CT);
+        finish_rows<EPI, CT>(p, n, tok0 + c * CT, nlive, v, es.rsm + c * CT, es.tpos + c * CT, es.trow + c * CT,
+                             lane, ew, es.sred, es.abest, es.stage + ew * 1024);
       }
+      if (whole) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+      } else if (et == 0) {
+        p.counters[tile] = 0u;
+      }
+      on_tile(et);
     }
     u += len;
   }
