@@ -190,6 +190,23 @@ int tc_smem_budget_kb() {
   return kb;
 }
 
+// Stream-K contributor caps of the forward's projections (qkv, o, gate/up, down, head):
+// how many CTAs may share one 128-row output tile, by token tile. A shared tile costs a
+// partial-sum round trip and a serial fix-up by its last contributor, which outweighs
+// the extra SMs streaming its weights except for the long-K down projection (K = 4864)
+// and for decode-sized QKV/o tiles; measured on the forward at batch 1-64 and 144-token
+// prefill. QI_TC_CAPS="a,b,c,d,e" overrides them for tuning experiments.
+void tc_caps(int caps[5], int NT) {
+  static int env[5] = {-1, 0, 0, 0, 0};
+  if (env[0] < 0) {
+    env[0] = 0;
+    if (const char* e = getenv("QI_TC_CAPS")) sscanf(e, "%d,%d,%d,%d,%d", &env[0], &env[1], &env[2], &env[3], &env[4]);
+  }
+  const int small[5] = {4, 4, 1, 8, 148};  // token tile <= 32 (decode)
+  const int large[5] = {1, 1, 1, 6, 148};  // token tile 64, 128 (large batches, prefill)
+  for (int i = 0; i < 5; ++i) caps[i] = env[0] > 0 ? (env[i] > 0 ? env[i] : 1) : (NT <= 32 ? small[i] : large[i]);
+}
+
 // Plan and launch one tensor-core projection: grid = min(SMs, units, scratch capacity),
 // pipeline stages within the shared-memory budget, TMEM for two accumulators.
 int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* counters, int counters_len,
@@ -255,6 +272,8 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     const int g = grid_for(p.n_mtiles * p.n_ntiles, p.KB, max_contrib);
     return run_tc(p, ws->tc_scratch, ws->tc_scratch_floats, ws->tc_counters, ws->tc_counters_len, g, s, pdl);
   };
+  int caps[5];
+  tc_caps(caps, NT);
   const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
   for (int li = 0; li < model->num_layers; ++li) {
     const qi_layer& L = model->layers[li];
@@ -277,7 +296,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.vc = vl;
     p.max_len = cache->max_len;
     p.cache_rows = cache->cache_rows;
-    if ((r = launch(p, 8)) != QI_OK) return r;
+    if ((r = launch(p, caps[0])) != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
                   ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, NT, cache->cache_rows);
     if (r != QI_OK) return r;
@@ -291,7 +310,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.next_norm_w = L.ln2;
     p.act_out = ws->act_x;
     p.ss_out = ws->ss;
-    if ((r = launch(p, 8)) != QI_OK) return r;
+    if ((r = launch(p, caps[1])) != QI_OK) return r;
     p = base;  // gate/up + SwiGLU
     p.w = L.w_gate_up;
     p.KB = kHidden / 64;
@@ -300,7 +319,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.ss_in = ws->ss;
     p.epi = kTcSwiglu;
     p.act_out = ws->act_h;
-    if ((r = launch(p, 148)) != QI_OK) return r;
+    if ((r = launch(p, caps[2])) != QI_OK) return r;
     p = base;  // down + residual; emits the next norm's inputs
     p.w = L.w_down;
     p.KB = kInter / 64;
@@ -311,7 +330,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.next_norm_w = li + 1 < model->num_layers ? model->layers[li + 1].ln1 : model->norm;
     p.act_out = ws->act_x;
     p.ss_out = ws->ss;
-    if ((r = launch(p, 12)) != QI_OK) return r;
+    if ((r = launch(p, caps[3])) != QI_OK) return r;
   }
   if (n_head > 0) {
     const int head_hi = head_lo + (n_head - 1) * head_stride + 1;
@@ -332,7 +351,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
       p.head_lo = head_lo;
       p.head_hi = head_hi;
       p.head_stride = head_stride;
-      if ((r = launch(p, 148)) != QI_OK) return r;
+      if ((r = launch(p, caps[4])) != QI_OK) return r;
     }
   }
   return QI_OK;
@@ -341,19 +360,6 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
 // Stage table of the persistent forward (forward_persistent.cu): the same projections,
 // epilogues, attention and embedding as forward_tc, each with the CTA subset and
 // completion target it uses, and the stage it waits for.
-// Contributor caps of the persistent forward's projections (qkv, o, gate/up, down, head);
-// QI_PERSIST_CAPS="a,b,c,d,e" overrides them for sweeps.
-void persistent_caps(int caps[5]) {
-  static int cached[5] = {0, 0, 0, 0, 0};
-  if (!cached[0]) {
-    int v[5] = {8, 8, 148, 12, 148};
-    if (const char* e = getenv("QI_PERSIST_CAPS"))
-      sscanf(e, "%d,%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3], &v[4]);
-    for (int i = 0; i < 5; ++i) cached[i] = v[i] > 0 ? v[i] : 1;
-  }
-  for (int i = 0; i < 5; ++i) caps[i] = cached[i];
-}
-
 int plan_persistent(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
                     const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
                     void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots,
@@ -377,7 +383,7 @@ int plan_persistent(const qi_model* model, const qi_cache* cache, const qi_works
   base.counters = ws->tc_counters;
   out.clear();
   int caps[5];
-  persistent_caps(caps);
+  tc_caps(caps, NT);  // the same partition as forward_tc: results are bitwise identical
   PStage e = {};
   e.kind = kPEmbed;
   e.dep = -1;
