@@ -65,8 +65,9 @@ def parse():
     ap.add_argument("--slots", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-seconds", type=float, default=15.0)
-    ap.add_argument("--only", choices=["roofline"], default=None,
-                    help="roofline: only the timed gate/up projection loop (the profiling case)")
+    ap.add_argument("--only", choices=["roofline", "decode"], default=None,
+                    help="roofline: only the timed gate/up projection loop; decode: only graph-replayed "
+                         "decode steps at --batch (the profiling cases)")
     ap.add_argument("--batch", type=int, default=22, help="decode batch of --only roofline")
     return ap.parse_args()
 
@@ -326,11 +327,30 @@ def kernel_roofline(model, M: int, pk: dict) -> dict:
     # of squares, SwiGLU activation tiles out (hi/lo bf16), for the M live tokens
     algo = 9728 * 896 * 2 + M * 896 * 4 + 7 * M * 4 + M * 4864 * 4
     gbs = algo / per_launch_s / 1e9
-    return {"kernel": "tc_proj_kernel<swiglu>: RMSNorm-folded gate/up projection + SwiGLU (tcgen05, stream-K, "
-                      "148 CTAs), the forward's largest weight stream", "bound": "hbm",
+    return {"kernel": "tc_proj_kernel<swiglu>: RMSNorm-folded gate/up projection + SwiGLU (tcgen05, bulk-copy "
+                      "ring, the forward's stream-K partition), the forward's largest weight stream", "bound": "hbm",
             "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"],
             "peak_source": pk["source"], "traffic": TRAFFIC.get(NT), "batch": M, "token_tile": NT,
             "us_per_launch": per_launch_s * 1e6, "algorithmic_bytes_per_launch": algo}
+
+
+def decode_steps(model, B: int, steps: int, warmup: int) -> dict:
+    """Graph-replayed decode steps of B rows at positions ~200 (the profiling case)."""
+    from qweninfer_b200.engine.kv_cache import KVCache
+    from qweninfer_b200.engine.runner import DecodeRunner
+    cache = KVCache(model.cfg, B, 512, dtype=torch.bfloat16, device=model.device)
+    r = DecodeRunner(model, cache, max_batch=B)
+    toks = [1] * B
+    for i in range(warmup):
+        r.decode(toks, [200 + i] * B)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        r.decode(toks, [200 + warmup + i] * B)
+    b.record()
+    b.synchronize()
+    r.check()
+    return {"batch": B, "steps": steps, "ms_per_step": a.elapsed_time(b) / steps}
 
 
 def batch1_latency(model) -> dict:
@@ -420,6 +440,9 @@ def main() -> None:
     torch.cuda.set_device(device)
     if args.only == "roofline":
         print(json.dumps(kernel_roofline(load_model(device), args.batch, peaks())), flush=True)
+        return
+    if args.only == "decode":
+        print(json.dumps(decode_steps(load_model(device), args.batch, args.steps, args.warmup)), flush=True)
         return
     if world > 1:
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)

@@ -287,7 +287,8 @@ int qi_tc_linear(const uint16_t* w, int n_rows, int K, const uint16_t* act, int 
  * interleaved tiled (9728, 896) weight, SwiGLU silu(gate) * up, written as activation
  * tiles (K = 4864, token tile NT) for the down projection: qwen2.py:114-116 with the
  * norm of qwen2.py:239. Same scratch/counter contract as qi_tc_linear (counters_len >=
- * 76 * ceil(M/NT)). act_out: ceil(M/NT) * NT * 4864 * 2 bf16. */
+ * 76 * ceil(M/NT)); ctas = 0 selects the stream-K partition qi_forward uses for this
+ * token tile. act_out: ceil(M/NT) * NT * 4864 * 2 bf16. */
 int qi_tc_gate_up_swiglu(const uint16_t* w_gate_up, const uint16_t* act, int M, int NT,
                          const float* ss, int ss_ld, float eps, uint16_t* act_out,
                          float* scratch, long long scratch_floats, unsigned int* counters,

@@ -716,6 +716,11 @@ int qi_tc_gate_up_swiglu(const uint16_t* w_gate_up, const uint16_t* act, int M, 
   p.epi = kTcSwiglu;
   p.act_out = act_out;
   p.err = err;
+  if (ctas <= 0) {  // the forward's partition
+    int caps[5];
+    tc_caps(caps, NT);
+    ctas = grid_for(p.n_mtiles * p.n_ntiles, p.KB, caps[2]);
+  }
   return run_tc(p, scratch, scratch_floats, counters, counters_len, ctas, as_stream(stream), false);
 }
 

@@ -266,6 +266,9 @@ def _split_plan(max_tokens: int, max_len: int) -> tuple[int, int]:
     """Key-split size and count for attention over `max_len` cache slots: fine splits
     (128 keys) when few queries must fill 148 SMs, coarse (1024) for prefill-sized M."""
     split = 128 if max_tokens <= 64 else 1024
+    import os
+    if os.environ.get("QI_ATTN_SPLIT"):  # tuning experiments: keys per split for every M
+        split = max(128, int(os.environ["QI_ATTN_SPLIT"]) // 128 * 128)
     split = max(split, -(-max_len // (128 * 128)) * 128)  # at most 128 splits (the merge's capacity)
     return split, max(1, -(-max_len // split))
 
