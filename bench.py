@@ -5,7 +5,8 @@ Workload (synthetic, seeded; no dataset): Qwen2-0.5B architecture (24 layers, hi
 requests arriving at t=0, prompts uniform in [32, 256] tokens, output lengths lognormal
 (median 75, sigma 0.8) clipped to [1, 256] and generated in full (no EOS); packed KV
 cache with max_len 512; 32 slots. One bench step = one complete run of the trace
-through `Engine.run` (96 B=1 prefills + every batched decode step + row moves).
+through `Engine.run` (the prefills of each step's admissions, batched into forwards of
+up to 512 tokens, + every batched decode step + row moves).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qweninfer_b200|reference]
 
@@ -146,8 +147,8 @@ class TimedRunner:
         self.decode_bytes = 0
         self.decode_rows = []
         self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-        self._prefill, self._decode = runner.prefill, runner.decode
-        runner.prefill, runner.decode = self.prefill, self.decode
+        self._prefill, self._prefill_many, self._decode = runner.prefill, runner.prefill_many, runner.decode
+        runner.prefill, runner.prefill_many, runner.decode = self.prefill, self.prefill_many, self.decode
 
     def prefill(self, row, prompt):
         self.ev[0].record()
@@ -156,6 +157,14 @@ class TimedRunner:
         self.ev[1].synchronize()
         self.device_ms += self.ev[0].elapsed_time(self.ev[1])
         return tok
+
+    def prefill_many(self, rows, prompts):
+        self.ev[0].record()
+        toks = self._prefill_many(rows, prompts)
+        self.ev[1].record()
+        self.ev[1].synchronize()
+        self.device_ms += self.ev[0].elapsed_time(self.ev[1])
+        return toks
 
     def decode(self, toks, pos, row_start=0):
         self.ev[0].record()

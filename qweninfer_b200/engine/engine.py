@@ -52,9 +52,10 @@ class Engine:
     def __init__(self, model, max_slots: int, max_len: int, eos_ids: set[int] | None = None,
                  static: bool = False, max_prefills_per_step: int | None = None,
                  pad_to: list[int] | None = None, cuda_graphs: bool = True,
-                 record: bool = False) -> None:
-        """engine.py:62-98. Extra keywords: `cuda_graphs` (capture each decode batch size)
-        and `record` (keep a per-step trace of scheduler actions in `self.trace`)."""
+                 record: bool = False, batch_prefill: bool = True) -> None:
+        """engine.py:62-98. Extra keywords: `cuda_graphs` (capture each decode batch size),
+        `record` (keep a per-step trace of scheduler actions in `self.trace`) and
+        `batch_prefill` (prefill a step's admissions together; same decisions)."""
         if pad_to is not None:
             if len(pad_to) <= max_slots or any(pad_to[n] < n for n in range(max_slots + 1)):
                 raise ValueError("pad_to needs an entry n -> size >= n for n = 0..max_slots")
@@ -66,6 +67,7 @@ class Engine:
         self.eos_ids = eos_ids or set()
         self.static = static
         self.max_prefills = max_prefills_per_step
+        self.batch_prefill = batch_prefill
         self.pad_to = pad_to
         self.waiting: deque[Request] = deque()
         self.active: list[Request] = []
@@ -89,27 +91,43 @@ class Engine:
         return len(req.output) >= req.max_new_tokens
 
     def _admit(self) -> list[Request]:
-        """engine.py:115-138: B = 1 prefill of waiting requests into row len(active)."""
+        """engine.py:115-138: prefill of waiting requests into row len(active), the same
+        requests into the same rows as the reference's one-at-a-time loop. Runs of
+        requests that keep their slot after prefill (no EOS ids, max_new_tokens > 1) are
+        prefilled together (runner.prefill_many); a request that may finish at its first
+        token is prefilled alone, because the next request reuses its row."""
         done = []
         if self.static and self.active:
             return done
         admitted = 0
         while (self.waiting and len(self.active) < self.max_slots
                and (self.max_prefills is None or admitted < self.max_prefills)):
-            req = self.waiting.popleft()
-            row, P = len(self.active), len(req.prompt)
-            self.cache.row_start, self.cache.window = row, P
-            tok = self.runner.prefill(row, req.prompt)
-            req.first_token = time.perf_counter()
-            admitted += 1
-            if self._rec is not None:
-                self._rec["admit"].append([req.rid, row, P, tok])
-            if self._finish_check(req, tok):
-                req.finished = req.first_token
-                done.append(req)
-                continue
-            req.length, req.last = P, tok
-            self.active.append(req)
+            run: list[Request] = []
+            if self.batch_prefill and not self.eos_ids:
+                while (self.waiting and len(self.active) + len(run) < self.max_slots
+                       and (self.max_prefills is None or admitted + len(run) < self.max_prefills)
+                       and self.waiting[0].max_new_tokens > 1):
+                    run.append(self.waiting.popleft())
+            if not run:
+                run = [self.waiting.popleft()]
+            rows = [len(self.active) + i for i in range(len(run))]
+            self.cache.row_start, self.cache.window = rows[-1], len(run[-1].prompt)
+            if len(run) > 1:
+                toks = self.runner.prefill_many(rows, [r.prompt for r in run])
+            else:
+                toks = [self.runner.prefill(rows[0], run[0].prompt)]
+            now = time.perf_counter()
+            for req, row, tok in zip(run, rows, toks):
+                req.first_token = now
+                admitted += 1
+                if self._rec is not None:
+                    self._rec["admit"].append([req.rid, row, len(req.prompt), tok])
+                if self._finish_check(req, tok):
+                    req.finished = req.first_token
+                    done.append(req)
+                    continue
+                req.length, req.last = len(req.prompt), tok
+                self.active.append(req)
         return done
 
     def _decode(self) -> list[int]:

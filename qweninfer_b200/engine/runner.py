@@ -124,6 +124,44 @@ class DecodeRunner:
         return int(self._read(1)[0])
 
     @torch.inference_mode()
+    def prefill_many(self, rows: list[int], prompts: list[list[int]]) -> list[int]:
+        """Prefill of several prompts, prompt i into cache row rows[i] at positions
+        0..P_i-1, in as few forwards as the staging capacity (cache.max_len tokens)
+        allows; returns each prompt's greedy next token. Every token attends to its own
+        row only, so this equals one prefill per prompt. In a forward the prompts' last
+        tokens are placed after all other tokens: the head tokens are then one contiguous
+        range (head_lo = M - n, stride 1)."""
+        if len(rows) != len(prompts) or len(set(rows)) != len(rows):
+            raise ValueError("one distinct cache row per prompt")
+        cap = self.cache.max_len
+        for row, p in zip(rows, prompts):
+            if not p or len(p) > cap:
+                raise ValueError(f"prompt length {len(p)} outside 1..{cap}")
+            if not 0 <= row < self.cache.max_batch:
+                raise IndexError(f"cache row {row} outside 0..{self.cache.max_batch - 1}")
+            self._check_ids(p)
+        out: list[int] = []
+        i = 0
+        while i < len(prompts):
+            j, tot = i, 0
+            while j < len(prompts) and tot + len(prompts[j]) <= cap:
+                tot += len(prompts[j])
+                j += 1
+            chunk, crow = prompts[i:j], rows[i:j]
+            n = len(chunk)
+            ids = [t for p in chunk for t in p[:-1]] + [p[-1] for p in chunk]
+            pos = [q for p in chunk for q in range(len(p) - 1)] + [len(p) - 1 for p in chunk]
+            rws = [r for r, p in zip(crow, chunk) for _ in range(len(p) - 1)] + list(crow)
+            M = len(ids)
+            self.pre.put(ids, pos, rws)
+            self.h2d_bytes += self.pre.h.numel() * 4
+            ws = self.model.workspace(cap, cap).plan(M)
+            self._forward(self.pre, M, ws, M - n, n)
+            out += [int(t) for t in self._read(n)]
+            i = j
+        return out
+
+    @torch.inference_mode()
     def decode(self, toks: list[int], pos: list[int], row_start: int = 0) -> np.ndarray:
         """One decode step: token toks[b] at position pos[b] of row row_start + b for every
         b < B; returns the B greedy tokens (engine.py:140-155)."""

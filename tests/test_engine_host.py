@@ -33,10 +33,16 @@ class StubCache:
 class StubRunner:
     def __init__(self, model, cache, max_batch, cuda_graphs=True):
         self.cache, self.max_batch = cache, max_batch
+        self.batches = []
 
     def prefill(self, row, prompt):
         assert 0 <= row < self.cache.max_batch
         return stub_token(prompt[-1], len(prompt) - 1, VOCAB)
+
+    def prefill_many(self, rows, prompts):
+        assert len(set(rows)) == len(rows)
+        self.batches.append(len(rows))
+        return [self.prefill(r, p) for r, p in zip(rows, prompts)]
 
     def decode(self, toks, pos, row_start=0):
         assert len(toks) <= self.max_batch
@@ -118,3 +124,29 @@ def test_eos_stops_without_appending():
     eng = StubEngine(fake_model(), max_slots=2, max_len=64, eos_ids={stub_token(5, 2, VOCAB)})
     done = eng.run([Request(0, [1, 2, 5], 10)])
     assert done[0].output == []
+
+
+def _trace_and_batches(reqs, **kw):
+    eng = StubEngine(fake_model(), record=True, **kw)
+    done = eng.run([Request(r.rid, list(r.prompt), r.max_new_tokens) for r in reqs])
+    return eng.trace, {r.rid: r.output for r in done}, eng.runner.batches
+
+
+@pytest.mark.parametrize("kw", [dict(max_slots=32, max_len=512),
+                                dict(max_slots=32, max_len=512, max_prefills_per_step=4),
+                                dict(max_slots=8, max_len=512, eos_ids={5, 77})])
+def test_batched_prefill_takes_the_same_decisions(kw):
+    """Prefilling a step's admissions together admits the same requests into the same
+    rows with the same first tokens as the one-at-a-time loop (engine.py:115-138),
+    including requests that finish at their first token (max_new_tokens = 1) and
+    configurations with EOS ids, which fall back to one prefill per request."""
+    reqs = [synthetic.SyntheticRequest(r.rid, r.prompt, 1 if r.rid % 7 == 3 else r.max_new_tokens)
+            for r in synthetic.serving96()[:48]]
+    t1, o1, b1 = _trace_and_batches(reqs, batch_prefill=True, **kw)
+    t0, o0, b0 = _trace_and_batches(reqs, batch_prefill=False, **kw)
+    assert t1 == t0 and o1 == o0
+    assert b0 == []
+    if "eos_ids" in kw:
+        assert b1 == []
+    else:
+        assert max(b1) > 1

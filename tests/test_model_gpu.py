@@ -249,3 +249,31 @@ def test_forward_writes_only_head_slots(gpu_model, persistent):
     ws.check()
     assert int(slots[0]) != sentinel
     assert bool((slots[1:] == sentinel).all())
+
+
+def test_prefill_many_matches_single_prefills(gpu_model):
+    """Several prompts in one forward (last tokens moved to the end) give the same greedy
+    tokens and the same cache rows as one B = 1 prefill each; the k-split of the
+    projections depends on the token count, so the cache agrees to bf16 rounding."""
+    from qweninfer_b200.engine.runner import DecodeRunner
+    rng = np.random.default_rng(31)
+    prompts = [rng.integers(0, gpu_model.cfg.vocab_size, n).tolist() for n in (1, 9, 64, 130, 7, 200)]
+    rows = [3, 0, 5, 1, 2, 4]
+    caches, toks = [], []
+    for many in (False, True):
+        cache = KVCache(gpu_model.cfg, 6, 512, dtype=torch.bfloat16, device="cuda")
+        r = DecodeRunner(gpu_model, cache, max_batch=6)
+        if many:
+            t = r.prefill_many(rows, prompts)
+        else:
+            t = [r.prefill(row, p) for row, p in zip(rows, prompts)]
+        r.check()
+        caches.append(cache)
+        toks.append(t)
+    assert toks[0] == toks[1]
+    for a, b in ((caches[0].k, caches[1].k), (caches[0].v, caches[1].v)):
+        a, b = a.float().flatten(1), b.float().flatten(1)  # (layer, everything else)
+        # per layer, relative to its largest value: fp32 reassociation drift (as for the
+        # hidden states) plus bf16 rounding; a misplaced token would be O(1)
+        err = (a - b).abs().amax(dim=1) / a.abs().amax(dim=1).clamp_min(1e-6)
+        assert bool((err <= HIDDEN_RTOL + 2 ** -8).all()), err.max().item()
