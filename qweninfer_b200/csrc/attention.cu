@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   }
   __syncthreads();
   uint32_t uses[2] = {0u, 0u};
-  attention_unit<false>(p, S, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, uses);
+  attention_unit<false, 8>(p, S, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, uses);
 }
 
 }  // namespace

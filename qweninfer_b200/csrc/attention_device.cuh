@@ -1,9 +1,13 @@
 // One attention work unit — (key split, KV head, query token) — as a device function shared
 // by the standalone attention kernel (attention.cu) and the persistent forward
-// (forward_persistent.cu). 128 threads (4 warps) run a unit; `sync` is the whole CTA in
-// the standalone kernel and a named barrier of the four epilogue warps in the persistent
-// one. The two K/V stage mbarriers are initialised once per CTA; `uses` carries their
-// phase counts from unit to unit.
+// (forward_persistent.cu). NW warps run a unit: warp w takes keys 32*(w % 4).. of every
+// 128-key tile and, with NW = 8, half of the 7 query heads (w / 4 picks the half). With
+// one CTA per SM the per-warp chain of dependent shared-memory loads, FMAs and shuffles
+// sets the tile time, so the standalone kernel uses 8 warps; the persistent forward runs
+// units on its 4 epilogue warps (NW = 4, all heads per warp). Every head's arithmetic is
+// the same in both forms. `sync` is the whole CTA in the standalone kernel and a named
+// barrier of the four epilogue warps in the persistent one. The two K/V stage mbarriers
+// are initialised once per CTA; `uses` carries their phase counts from unit to unit.
 #pragma once
 
 #include "common.cuh"
@@ -13,7 +17,7 @@
 namespace qi {
 namespace attn {
 
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = 256;  // the standalone kernel (NW = 8)
 constexpr int kTile = 128;  // keys per stage
 constexpr int kPartStride = kGqa * (kHeadDim + 2);  // floats per (token, head, split) partial
 static_assert(2 * kGqa * kMaxAttnSplits + kGqa <= 4 * kGqa * (kHeadDim + 2), "split merge scratch");
@@ -22,8 +26,8 @@ struct AttnSmem {
   uint16_t k[2][kTile * kHeadDim];
   uint16_t v[2][kTile * kHeadDim];
   float q[kGqa * 2 * 8 * 4];          // per head: [half][chunk][4], scaled by 1/sqrt(64)
-  float p[4][32][8];                  // per warp: probabilities of its 32 keys, 7 heads
-  float cmb[4][kGqa][kHeadDim + 2];   // per warp: acc[64], m, l
+  float p[4][32][8];                  // per key group: probabilities of its 32 keys, 7 heads
+  float cmb[4][kGqa][kHeadDim + 2];   // per key group and head: acc[64], m, l
   uint64_t bar[2];
   int last;
 };
@@ -41,15 +45,22 @@ __device__ __forceinline__ void emit(const AttnParams& p, int tok, int f, float 
 
 // Runs unit (split, g, tok); returns true when it wrote the final output of (tok, g)
 // (a single split, or the last split to arrive, which merges all of them).
-template <bool kNamedBarrier>
+template <bool kNamedBarrier, int NW>
 __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S, int split, int g, int tok,
                                                int tid, uint32_t (&uses)[2]) {
+  static_assert(NW == 4 || NW == 8, "4 or 8 warps");
+  static_assert(!kNamedBarrier || NW == 4, "the named barrier spans 4 warps");
+  constexpr int NT = NW * 32;
+  constexpr int HPG = NW == 4 ? kGqa : (kGqa + 1) / 2;  // heads per warp
   auto sync = [] {
     if constexpr (kNamedBarrier) asm volatile("bar.sync 1, 128;" ::: "memory");
     else __syncthreads();
   };
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  const int kgrp = warp & 3;                // key group: keys 32 * kgrp .. of each tile
+  const int h0 = (warp >> 2) * HPG;         // first head of this warp
+  const int nh = min(HPG, kGqa - h0);       // heads of this warp
   const int ps = p.pos[tok];
   const int row = p.rows[tok];
   if (ps < 0 || ps >= p.max_len || row < 0 || (p.cache_rows > 0 && row >= p.cache_rows)) {
@@ -71,16 +82,16 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   // eight 8-dim chunks' first halves are 16-byte neighbours (conflict-free rotated reads).
   // (all four loads of a thread are issued before its shared-memory stores)
   {
-    constexpr int kRounds = (kGqa * kHeadDim + kAttnThreads - 1) / kAttnThreads;
+    constexpr int kRounds = (kGqa * kHeadDim + NT - 1) / NT;
     float qv[kRounds];
 #pragma unroll
     for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * kAttnThreads;
+      const int idx = tid + r * NT;
       qv[r] = __ldcg(p.q + (long long)tok * kHidden + g * kGqa * kHeadDim + (idx < kGqa * kHeadDim ? idx : 0));
     }
 #pragma unroll
     for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * kAttnThreads;
+      const int idx = tid + r * NT;
       if (idx < kGqa * kHeadDim) {
         const int h = idx >> 6, d = idx & 63;
         const int cc = d >> 3, e = d & 7;
@@ -110,12 +121,12 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     if (ntiles > 1) issue(1);
   }
 
-  float m[kGqa], l[kGqa], acc[kGqa][2];
+  float m[HPG], l[HPG], acc[HPG][2];
 #pragma unroll
-  for (int h = 0; h < kGqa; ++h) {
-    m[h] = -INFINITY;
-    l[h] = 0.f;
-    acc[h][0] = acc[h][1] = 0.f;
+  for (int hi = 0; hi < HPG; ++hi) {
+    m[hi] = -INFINITY;
+    l[hi] = 0.f;
+    acc[hi][0] = acc[hi][1] = 0.f;
   }
 
   for (int i = 0; i < ntiles; ++i) {
@@ -123,13 +134,13 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     mbar_wait(&S.bar[st], parity(i), p.err);
     const int k0 = kbeg + i * kTile;
     const int nk = min(kTile, kend - k0);
-    const int kw = 32 * warp;
+    const int kw = 32 * kgrp;
     const int nkw = max(0, min(32, nk - kw));
     if (nkw > 0) {
       const bool valid = lane < nkw;
-      float s[kGqa];
+      float s[HPG];
 #pragma unroll
-      for (int h = 0; h < kGqa; ++h) s[h] = 0.f;
+      for (int hi = 0; hi < HPG; ++hi) s[hi] = 0.f;
       const uint16_t* krow = S.k[st] + (kw + lane) * kHeadDim;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
@@ -138,47 +149,58 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
         const float k0f = bf16lo(kv.x), k1f = bf16hi(kv.x), k2f = bf16lo(kv.y), k3f = bf16hi(kv.y);
         const float k4f = bf16lo(kv.z), k5f = bf16hi(kv.z), k6f = bf16lo(kv.w), k7f = bf16hi(kv.w);
 #pragma unroll
-        for (int h = 0; h < kGqa; ++h) {
-          const float4 qa = *reinterpret_cast<const float4*>(&S.q[((h * 2 + 0) * 8 + cc) * 4]);
-          const float4 qb = *reinterpret_cast<const float4*>(&S.q[((h * 2 + 1) * 8 + cc) * 4]);
-          float a = s[h];
-          a = fmaf(qa.x, k0f, a);
-          a = fmaf(qa.y, k1f, a);
-          a = fmaf(qa.z, k2f, a);
-          a = fmaf(qa.w, k3f, a);
-          a = fmaf(qb.x, k4f, a);
-          a = fmaf(qb.y, k5f, a);
-          a = fmaf(qb.z, k6f, a);
-          a = fmaf(qb.w, k7f, a);
-          s[h] = a;
+        for (int hi = 0; hi < HPG; ++hi) {
+          if (hi < nh) {
+            const int h = h0 + hi;
+            const float4 qa = *reinterpret_cast<const float4*>(&S.q[((h * 2 + 0) * 8 + cc) * 4]);
+            const float4 qb = *reinterpret_cast<const float4*>(&S.q[((h * 2 + 1) * 8 + cc) * 4]);
+            float a = s[hi];
+            a = fmaf(qa.x, k0f, a);
+            a = fmaf(qa.y, k1f, a);
+            a = fmaf(qa.z, k2f, a);
+            a = fmaf(qa.w, k3f, a);
+            a = fmaf(qb.x, k4f, a);
+            a = fmaf(qb.y, k5f, a);
+            a = fmaf(qb.z, k6f, a);
+            a = fmaf(qb.w, k7f, a);
+            s[hi] = a;
+          }
         }
       }
 #pragma unroll
-      for (int h = 0; h < kGqa; ++h) {
-        const float sv = valid ? s[h] : -INFINITY;
-        const float mn = fmaxf(m[h], warp_max(sv));
-        const float alpha = expf(m[h] - mn);
-        const float pr = valid ? expf(sv - mn) : 0.f;
-        l[h] = l[h] * alpha + warp_sum(pr);
-        acc[h][0] *= alpha;
-        acc[h][1] *= alpha;
-        m[h] = mn;
-        S.p[warp][lane][h] = pr;
+      for (int hi = 0; hi < HPG; ++hi) {
+        if (hi < nh) {
+          const float sv = valid ? s[hi] : -INFINITY;
+          const float mn = fmaxf(m[hi], warp_max(sv));
+          const float alpha = expf(m[hi] - mn);
+          const float pr = valid ? expf(sv - mn) : 0.f;
+          l[hi] = l[hi] * alpha + warp_sum(pr);
+          acc[hi][0] *= alpha;
+          acc[hi][1] *= alpha;
+          m[hi] = mn;
+          S.p[kgrp][lane][h0 + hi] = pr;
+        }
       }
       __syncwarp();
       const uint16_t* vt = S.v[st] + kw * kHeadDim + 2 * lane;
+#pragma unroll 4
       for (int j = 0; j < nkw; ++j) {
         const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vt + j * kHeadDim);
         const float v0 = bf16lo(v2), v1 = bf16hi(v2);
-        const float4 pa = *reinterpret_cast<const float4*>(&S.p[warp][j][0]);
-        const float4 pb = *reinterpret_cast<const float4*>(&S.p[warp][j][4]);
-        acc[0][0] = fmaf(pa.x, v0, acc[0][0]); acc[0][1] = fmaf(pa.x, v1, acc[0][1]);
-        acc[1][0] = fmaf(pa.y, v0, acc[1][0]); acc[1][1] = fmaf(pa.y, v1, acc[1][1]);
-        acc[2][0] = fmaf(pa.z, v0, acc[2][0]); acc[2][1] = fmaf(pa.z, v1, acc[2][1]);
-        acc[3][0] = fmaf(pa.w, v0, acc[3][0]); acc[3][1] = fmaf(pa.w, v1, acc[3][1]);
-        acc[4][0] = fmaf(pb.x, v0, acc[4][0]); acc[4][1] = fmaf(pb.x, v1, acc[4][1]);
-        acc[5][0] = fmaf(pb.y, v0, acc[5][0]); acc[5][1] = fmaf(pb.y, v1, acc[5][1]);
-        acc[6][0] = fmaf(pb.z, v0, acc[6][0]); acc[6][1] = fmaf(pb.z, v1, acc[6][1]);
+        float pv[HPG];
+        if constexpr (HPG == 4) {
+          const float4 pa = *reinterpret_cast<const float4*>(&S.p[kgrp][j][h0]);
+          pv[0] = pa.x; pv[1] = pa.y; pv[2] = pa.z; pv[3] = pa.w;
+        } else {
+          const float4 pa = *reinterpret_cast<const float4*>(&S.p[kgrp][j][0]);
+          const float4 pb = *reinterpret_cast<const float4*>(&S.p[kgrp][j][4]);
+          pv[0] = pa.x; pv[1] = pa.y; pv[2] = pa.z; pv[3] = pa.w; pv[4] = pb.x; pv[5] = pb.y; pv[6] = pb.z;
+        }
+#pragma unroll
+        for (int hi = 0; hi < HPG; ++hi) {
+          acc[hi][0] = fmaf(pv[hi], v0, acc[hi][0]);
+          acc[hi][1] = fmaf(pv[hi], v1, acc[hi][1]);
+        }
       }
       __syncwarp();
     }
@@ -186,19 +208,22 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     if (tid == 0 && i + 2 < ntiles) issue(i + 2);
   }
 
-  // Merge the 4 warps.
+  // Merge the 4 key groups.
 #pragma unroll
-  for (int h = 0; h < kGqa; ++h) {
-    S.cmb[warp][h][2 * lane] = acc[h][0];
-    S.cmb[warp][h][2 * lane + 1] = acc[h][1];
-    if (lane == 0) {
-      S.cmb[warp][h][kHeadDim] = m[h];
-      S.cmb[warp][h][kHeadDim + 1] = l[h];
+  for (int hi = 0; hi < HPG; ++hi) {
+    if (hi < nh) {
+      const int h = h0 + hi;
+      S.cmb[kgrp][h][2 * lane] = acc[hi][0];
+      S.cmb[kgrp][h][2 * lane + 1] = acc[hi][1];
+      if (lane == 0) {
+        S.cmb[kgrp][h][kHeadDim] = m[hi];
+        S.cmb[kgrp][h][kHeadDim + 1] = l[hi];
+      }
     }
   }
   sync();
   float* part = p.part + (((long long)tok * kKvHeads + g) * p.max_splits + split) * kPartStride;
-  for (int idx = tid; idx < kGqa * (kHeadDim + 2); idx += kAttnThreads) {
+  for (int idx = tid; idx < kGqa * (kHeadDim + 2); idx += NT) {
     const int h = idx / (kHeadDim + 2);
     const int d = idx - h * (kHeadDim + 2);
     float mx = -INFINITY;
@@ -232,7 +257,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   // area: 2 * 7 * nsplit + 7 floats), (2) per head the max and the split weights
   // exp(m_s - max), (3) the weighted sum of the split outputs, loads before stores.
   float* sm = &S.cmb[0][0][0];
-  for (int idx = tid; idx < kGqa * nsplit; idx += kAttnThreads) {
+  for (int idx = tid; idx < kGqa * nsplit; idx += NT) {
     const int h = idx / nsplit, s = idx - h * nsplit;
     const float* ph = base + s * kPartStride + h * (kHeadDim + 2);
     const float mv = __ldcg(ph + kHeadDim), lv = __ldcg(ph + kHeadDim + 1);
@@ -254,7 +279,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   }
   sync();
   {
-    constexpr int kRounds = (kGqa * kHeadDim + kAttnThreads - 1) / kAttnThreads;
+    constexpr int kRounds = (kGqa * kHeadDim + NT - 1) / NT;
     float A[kRounds];
 #pragma unroll
     for (int r = 0; r < kRounds; ++r) A[r] = 0.f;
@@ -263,7 +288,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
       const float* ps = base + s * kPartStride;
 #pragma unroll
       for (int r = 0; r < kRounds; ++r) {
-        const int idx = tid + r * kAttnThreads;
+        const int idx = tid + r * NT;
         if (idx < kGqa * kHeadDim) {
           const int h = idx >> 6, d = idx & 63;
           A[r] = fmaf(sm[h * nsplit + s], __ldcg(ps + h * (kHeadDim + 2) + d), A[r]);
@@ -272,7 +297,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     }
 #pragma unroll
     for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * kAttnThreads;
+      const int idx = tid + r * NT;
       if (idx < kGqa * kHeadDim) emit(p, tok, g * kGqa * kHeadDim + idx, A[r] / sm[2 * kGqa * nsplit + (idx >> 6)]);
     }
   }

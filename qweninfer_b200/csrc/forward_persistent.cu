@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_forward_kernel(const P
           const int tok = u % a.M;
           const int g = (u / a.M) % kKvHeads;
           const int split = u / (a.M * kKvHeads);
-          if (attention_unit<true>(a, AS, split, g, tok, et, uses)) signal_done(dn, et);
+          if (attention_unit<true, 4>(a, AS, split, g, tok, et, uses)) signal_done(dn, et);
         }
       } else {
         const TcParams& p = st.tc;
