@@ -329,14 +329,17 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
       // publish this CTA's partial sum of the tile, then arrive on the tile's counter
       // (acq_rel: releases the partial stores of all 128 threads, ordered before it by the
       // barrier, and acquires the other contributors' if this arrival is the last)
+      // partial layout per (CTA, slot): [column / 4][row][column % 4], so the 32 lanes
+      // (consecutive rows) of a warp store or load 512 contiguous bytes per float4
       const int slot = (geo.start(cta) >= tile * p.KB) ? 0 : 1;
-      float* my_part = p.scratch + (((long long)cta * 2 + slot) * 128 + row) * NT;
+      float* my_part = p.scratch + ((long long)cta * 2 + slot) * 128 * NT + row * 4;
       for (int c = 0; c < nchunks; ++c) {
         float v[CT];
         tmem_chunk(c, v);
         const int nlive = min(CT, live - c * CT);
         for (int i = 0; i < nlive; i += 4)
-          *reinterpret_cast<float4*>(my_part + c * CT + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          *reinterpret_cast<float4*>(my_part + (long long)((c * CT + i) >> 2) * 512) =
+              make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
       }
       tc_fence_before();
       __syncwarp();
@@ -361,10 +364,11 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
           const int cc = cc0 + a;
           const bool on = cc <= c_last;
           const int slot = (geo.start(on ? cc : c_first) >= tile * p.KB) ? 0 : 1;
-          const float* src = p.scratch + (((long long)(on ? cc : c_first) * 2 + slot) * 128 + row) * NT + c * CT;
+          const float* src = p.scratch + ((long long)(on ? cc : c_first) * 2 + slot) * 128 * NT + row * 4 +
+                              (long long)((c * CT) >> 2) * 512;
 #pragma unroll
           for (int i4 = 0; i4 < CT / 4; ++i4)
-            q[a][i4] = (on && 4 * i4 < nlive) ? __ldcg(reinterpret_cast<const float4*>(src + 4 * i4))
+            q[a][i4] = (on && 4 * i4 < nlive) ? __ldcg(reinterpret_cast<const float4*>(src + i4 * 512))
                                               : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       };

@@ -263,9 +263,11 @@ class Block(nn.Module):
 # ------------------------------------------------------------- scratch space
 
 def _split_plan(max_tokens: int, max_len: int) -> tuple[int, int]:
-    """Key-split size and count for attention over `max_len` cache slots: fine splits
-    (128 keys) when few queries must fill 148 SMs, coarse (1024) for prefill-sized M."""
-    split = 128 if max_tokens <= 64 else 1024
+    """Key-split size and count for attention over `max_len` cache slots: 256 keys per
+    split when few queries must fill 148 SMs (measured best over 128/256/512 at decode
+    batches 1-64: finer splits pay a split-merge round trip, coarser ones serialise
+    tiles), coarse (1024) for prefill-sized M."""
+    split = 256 if max_tokens <= 64 else 1024
     import os
     if os.environ.get("QI_ATTN_SPLIT"):  # tuning experiments: keys per split for every M
         split = max(128, int(os.environ["QI_ATTN_SPLIT"]) // 128 * 128)
