@@ -230,24 +230,33 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
       epi_bar();
     }
   } else {  // kTcLogits: tied head (qwen2.py:282-292) + greedy argmax (engine.py:155)
+    // the chunk's tokens reduce as independent butterflies (one chain per token would
+    // serialise 16 x 5 dependent shuffle pairs); a token counts only if it is a live
+    // head token
+    unsigned long long key[CT];
 #pragma unroll
     for (int i = 0; i < CT; ++i) {
-      if (i >= nlive) break;
       const int t = tbase + i;
-      if (t < p.head_lo || t >= p.head_hi || (t - p.head_lo) % p.head_stride) continue;
       const float x = v[i] * rs[i];
-      if (p.logits) {
+      const bool head = i < nlive && t >= p.head_lo && t < p.head_hi && (t - p.head_lo) % p.head_stride == 0;
+      if (head && p.logits) {
         const long long o = (long long)((t - p.head_lo) / p.head_stride) * p.logits_ld + n;
         if (p.logits_bf16) reinterpret_cast<uint16_t*>(p.logits)[o] = f32_to_bf16_rn(x);
         else reinterpret_cast<float*>(p.logits)[o] = x;
       }
-      unsigned long long key = argmax_pack(x, n);
+      key[i] = head ? argmax_pack(x, n) : 0ull;
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-        key = other > key ? other : key;
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < CT; ++i) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key[i], o);
+        key[i] = other > key[i] ? other : key[i];
       }
-      if (lane == 0) atomicMax(&abest[t & (p.NT - 1)], key);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < CT; ++i)
+        if (key[i]) atomicMax(&abest[(tbase + i) & (p.NT - 1)], key[i]);
     }
   }
 }
