@@ -170,8 +170,25 @@ bool bad_ptr(const void* p) { return p == nullptr; }
 inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
 inline bool bad_nt(int NT) { return NT < 8 || NT > 128 || (NT & (NT - 1)) != 0; }
 
-// Token tile of a forward over M tokens: the power of two >= M (at least 8), at most 128.
+// Token tile of a forward over M tokens: 8 up to 8 tokens, 16 up to 96, 32 up to 384,
+// 64 beyond (measured on decode batches 22-64 and prefills of 32-512 tokens: about four
+// or more token tiles keep more CTAs busy without splitting tiles along K and keep each
+// tile's epilogue short). Non-decreasing in M, so a workspace sized for its largest token
+// count covers every smaller forward. QI_MAX_TOKEN_TILE (8..128) caps it for tuning.
 inline int token_tile(int M) {
+  static int cap = -1;
+  if (cap < 0) {
+    const char* e = getenv("QI_MAX_TOKEN_TILE");
+    const int v = e ? atoi(e) : 128;
+    cap = (v >= 8 && v <= 128 && (v & (v - 1)) == 0) ? v : 128;
+  }
+  const int nt = M <= 8 ? 8 : M <= 96 ? 16 : M <= 384 ? 32 : 64;
+  return nt < cap ? nt : cap;
+}
+
+// Token tile of the persistent forward: one tile covers all M <= 128 tokens (the power of
+// two >= M, at least 8); its stage table has a single token tile per projection.
+inline int persist_tile(int M) {
   int nt = 8;
   while (nt < M && nt < 128) nt <<= 1;
   return nt;
@@ -364,7 +381,7 @@ int plan_persistent(const qi_model* model, const qi_cache* cache, const qi_works
                     const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
                     void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots,
                     std::vector<PStage>& out) {
-  const int NT = token_tile(M);
+  const int NT = persist_tile(M);
   if (M > 128 || M > ws->ss_ld || !ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss || !ws->tc_scratch ||
       !ws->tc_counters || !ws->err)
     return QI_ERR_ARG;
@@ -517,7 +534,7 @@ int launch_persistent_table(const void* table, int n_stages, const qi_workspace*
   P.n_stages = n_stages;
   P.done = ws->persist_done;
   P.M = M;
-  P.NT = token_tile(M);
+  P.NT = persist_tile(M);
   P.ring = persistent_ring(P.NT);
   uint32_t cols = 32;
   while (cols < (uint32_t)(4 * P.NT)) cols <<= 1;

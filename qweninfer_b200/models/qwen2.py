@@ -287,11 +287,10 @@ class _AttnScratch:
 
 
 def token_tile(M: int) -> int:
-    """Token tile of the tensor-core projections: power of two >= M, between 8 and 128."""
-    nt = 8
-    while nt < M and nt < 128:
-        nt *= 2
-    return nt
+    """Token tile of the forward's tensor-core projections for M tokens (the rule of
+    token_tile in csrc/api.cu): 8 up to 8 tokens, 16 up to 96, 32 up to 384, 64 beyond.
+    Non-decreasing in M, so buffers sized for max_tokens cover every smaller forward."""
+    return 8 if M <= 8 else 16 if M <= 96 else 32 if M <= 384 else 64
 
 
 def use_persistent(M: int) -> bool:
@@ -360,7 +359,8 @@ class Workspace:
         self.attn_counters = torch.zeros(max_tokens * 2, dtype=torch.int32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         # tensor-core path: activation tiles (hi/lo bf16), sums of squares, stream-K scratch
-        nt = token_tile(max_tokens)
+        # sized for the forward's token tile and for the persistent forward's single tile
+        nt = max(token_tile(max_tokens), 8 if max_tokens <= 8 else min(128, 1 << (max_tokens - 1).bit_length()))
         pad = -(-max_tokens // nt) * nt
         bf = dict(dtype=torch.bfloat16, device=device)
         self.act_x = torch.zeros(pad * HIDDEN * 2, **bf)
@@ -369,7 +369,7 @@ class Workspace:
         self.ss = torch.zeros(7 * pad, **f32)
         sms = torch.cuda.get_device_properties(device).multi_processor_count
         self.tc_scratch = torch.empty(sms * 2 * 128 * nt, **f32)
-        n_counters = max(76 * (pad // nt), -(-vocab // 128), 64)
+        n_counters = max(76 * -(-pad // 8), -(-vocab // 128), 64)  # any token tile down to 8
         self.tc_counters = torch.zeros(n_counters, dtype=torch.int32, device=device)
         self.persist_done = torch.zeros(512 * 32, dtype=torch.int32, device=device)  # 512 stages, 128 B apart
         self.persist_trace = torch.zeros(513, dtype=torch.int64, device=device)

@@ -16,7 +16,17 @@ import torch
 
 from oracle import bf16_round, rmsnorm
 from qweninfer_b200 import _lib
-from qweninfer_b200.models.qwen2 import tile_weight, token_tile
+from qweninfer_b200.models.qwen2 import tile_weight
+
+
+def token_tile(M: int) -> int:
+    """Every valid token tile is exercised: the power of two >= M, 8..128 (the forward's own
+    choice is smaller; the kernels accept any of them)."""
+    nt = 8
+    while nt < M and nt < 128:
+        nt *= 2
+    return nt
+
 
 DEV = "cuda"
 _KEEP: list[torch.Tensor] = []
