@@ -294,19 +294,19 @@ __global__ void __launch_bounds__(kThreads, 1) persistent_forward_kernel(const P
         auto on_tile = [&](int e) { signal_done(dn, e); };
         switch (p.epi) {
           case kTcQkvRope:
-            epilogue_range<kTcQkvRope>(p, geo, c, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
+            epilogue_range<kTcQkvRope, 4>(p, geo, c, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
                                        on_tile);
             break;
           case kTcResidual:
-            epilogue_range<kTcResidual>(p, geo, c, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
+            epilogue_range<kTcResidual, 4>(p, geo, c, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
                                         on_tile);
             break;
           case kTcSwiglu:
-            epilogue_range<kTcSwiglu>(p, geo, c, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
+            epilogue_range<kTcSwiglu, 4>(p, geo, c, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
                                       on_tile);
             break;
           default:
-            epilogue_range<kTcLogits>(p, geo, c, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
+            epilogue_range<kTcLogits, 4>(p, geo, c, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
                                       on_tile);
             break;
         }

@@ -11,7 +11,9 @@
 namespace qi {
 namespace tc {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;        // producer, MMA issuer, 4 epilogue warps (persistent kernel)
+constexpr int kProjEpiWarps = 8;      // epilogue warps of tc_proj_kernel: two per TMEM lane quadrant
+constexpr int kProjThreads = 64 + 32 * kProjEpiWarps;
 constexpr int kEpiWarp0 = 2;
 constexpr uint32_t kABytes = 128 * 64 * 2;  // one 128x64 weight block
 
@@ -56,6 +58,21 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 }
 // named barrier of the four epilogue warps
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barrier of EW epilogue warps
+template <int EW>
+__device__ __forceinline__ void epi_bar_n() {
+  if constexpr (EW == 4) asm volatile("bar.sync 1, 128;" ::: "memory");
+  else asm volatile("bar.sync 1, 256;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
 
 // SWIZZLE_NONE K-major shared-memory descriptor: LBO 128 B, SBO 1024 B, version bit (sm_100).
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
@@ -82,24 +99,24 @@ struct Geom {
 // Shared-memory scratch of the four epilogue warps (carve_epi lays it out).
 struct EpiSmem {
   unsigned long long* abest;  // 128 packed argmax candidates of the token tile
-  float* sred;                // 4 x 16 per-warp partial sums of squares
+  float* sred;                // [4 lane quadrants][128 tokens] partial sums of squares
   float* rsm;                 // 128 per-token reciprocal RMS of the current token tile
   int* tpos;                  // 128 positions of the current token tile
   int* trow;                  // 128 cache rows of the current token tile
   int* flag;                  // last-contributor broadcast
-  uint16_t* stage;            // 4 x 1024: per-warp staging of activation-tile stores
+  uint16_t* stage;            // 4096: per-warp staging of activation-tile stores
 };
-constexpr size_t kEpiSmemBytes = 128 * 8 + 64 * 4 + 128 * 4 + 128 * 4 + 128 * 4 + 16 + 4 * 1024 * 2;
+constexpr size_t kEpiSmemBytes = 128 * 8 + 4 * 128 * 4 + 128 * 4 + 128 * 4 + 128 * 4 + 16 + 4096 * 2;
 
 __device__ __forceinline__ EpiSmem carve_epi(uint8_t* base) {  // base 8-byte aligned
   EpiSmem e;
   e.abest = reinterpret_cast<unsigned long long*>(base);
   e.sred = reinterpret_cast<float*>(base + 1024);
-  e.rsm = e.sred + 64;
+  e.rsm = e.sred + 4 * 128;
   e.tpos = reinterpret_cast<int*>(e.rsm + 128);
   e.trow = e.tpos + 128;
   e.flag = e.trow + 128;
-  e.stage = reinterpret_cast<uint16_t*>(base + 2832);  // 16-byte aligned when base is
+  e.stage = reinterpret_cast<uint16_t*>(base + 4624);  // 16-byte aligned when base is
   return e;
 }
 
@@ -219,16 +236,9 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
       p.x[(long long)t * kHidden + n] = xv;
       an[i] = xv * wn;
       const float s = warp_sum(xv * xv);
-      if (lane == 0) sred[ew * 16 + i] = s;
+      if (lane == 0) sred[i] = s;  // this lane quadrant's partial of token tbase + i
     }
     if (p.act_out) act_store_warp<CT, 0>(p.act_out, kHidden, p.NT, p.lg_nt, n - lane, tbase, nlive, an, wbuf, lane);
-    if (p.ss_out) {
-      epi_bar();
-      if (ew == 0 && lane < nlive)
-        p.ss_out[(long long)(n >> 7) * p.ss_ld + tbase + lane] =
-            (sred[lane] + sred[16 + lane]) + (sred[32 + lane] + sred[48 + lane]);
-      epi_bar();
-    }
   } else {  // kTcLogits: tied head (qwen2.py:282-292) + greedy argmax (engine.py:155)
     // the chunk's tokens reduce as independent butterflies (one chain per token would
     // serialise 16 x 5 dependent shuffle pairs); a token counts only if it is a live
@@ -261,23 +271,29 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
   }
 }
 
-// Epilogue of a CTA's stream-K units [u0, u1) of one projection, run by the four
-// epilogue warps: per segment (the CTA's part of one output tile) wait for the MMA
-// warp's accumulator, then either finish the tile (whole segment) or publish the
-// partial sum and, if this CTA arrives last on the tile's counter, add all partials in
-// k order (deterministic) and finish it. on_tile(et) runs on the 128 threads after a
-// tile's final outputs are written. `seg` counts the CTA's segments (accumulator buffer
-// b = seg & 1) and carries over between calls.
-template <int EPI, class OnTile>
+// Epilogue of a CTA's stream-K units [u0, u1) of one projection, run by EW epilogue warps
+// (4 or 8). Warp w reads TMEM lane quadrant w % 4 (rows 32 * (w % 4) ..) and, with 8
+// warps, the token chunks c = w / 4, w / 4 + 2, .. of CT columns, so two warps share each
+// sub-partition and hide each other's latencies. Per segment (the CTA's part of one
+// output tile): wait for the MMA warp's accumulator, then either finish the tile (whole
+// segment) or publish the partial sum and, if this CTA arrives last on the tile's
+// counter, add all partials in k order (deterministic) and finish it. on_tile(et) runs
+// on the epilogue threads after a tile's final outputs are written. `seg` counts the
+// CTA's segments (accumulator buffer b = seg & 1) and carries over between calls.
+template <int EPI, int EW, class OnTile>
 __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& geo, int cta, int u0, int u1, int& seg,
                                                uint64_t* acc_full, uint64_t* acc_empty, uint32_t tmem_base, int N,
                                                int warp, int lane, const EpiSmem& es, OnTile on_tile) {
-  constexpr int CT = 16;
+  static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
+  constexpr int CT = EW == 8 ? 8 : 16;  // token columns per chunk
+  constexpr int CSTEP = EW / 4;         // chunk stride of one warp
   const int NT = p.NT;
   const int ew = warp - kEpiWarp0;
   const int quad = warp & 3;
+  const int cfirst = ew / 4;            // this warp's first chunk
   const int row = quad * 32 + lane;
   const int et = ew * 32 + lane;
+  uint16_t* wbuf = es.stage + ew * (4096 / EW);
   int cur_nt = -1;
   for (int u = u0; u < u1; ++seg) {
     const int tile = u / p.KB, kb0 = u - tile * p.KB;
@@ -292,8 +308,8 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
       // per-token reciprocal RMS of this token tile (RMSNorm.forward, qwen2.py:44-48) from
       // the producer's 7 partial sums of squares (1 for unnormalised inputs), and for the
       // QKV epilogue the tokens' positions and cache rows; staged while the MMAs run
-      epi_bar();
-      {  // every entry is written (tokens past `live`: neutral values)
+      epi_bar_n<EW>();
+      if (et < 128) {  // every entry is written (tokens past `live`: neutral values)
         float r = 1.0f;
         if (p.ss_in && et < live) {
           float ss = 0.f;
@@ -308,7 +324,7 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
         }
       }
       cur_nt = ntile;
-      epi_bar();
+      epi_bar_n<EW>();
     }
     const int b = seg & 1;
     mbar_wait(&acc_full[b], (uint32_t)((seg >> 1) & 1), p.err);
@@ -317,32 +333,40 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
     const int nchunks = (min(NT, live) + CT - 1) / CT;
     // accumulator chunk c (columns c*CT..) with its hi and lo halves summed
     auto tmem_chunk = [&](int c, float (&v)[CT]) {
-      float r[16];
-      if (NT == 8) {
-        tmem_ld16(t_base, r);
+      if constexpr (CT == 16) {
+        float r[16];
+        if (NT == 8) {
+          tmem_ld16(t_base, r);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = r[i] + r[8 + i];
+          for (int i = 0; i < 8; ++i) v[i] = r[i] + r[8 + i];
 #pragma unroll
-        for (int i = 8; i < 16; ++i) v[i] = 0.f;
+          for (int i = 8; i < 16; ++i) v[i] = 0.f;
+        } else {
+          float lo[16];
+          tmem_ld16(t_base + (uint32_t)(c * CT), r);
+          tmem_ld16(t_base + (uint32_t)(NT + c * CT), lo);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = r[i] + lo[i];
+        }
       } else {
-        float lo[16];
-        tmem_ld16(t_base + (uint32_t)(c * CT), r);
-        tmem_ld16(t_base + (uint32_t)(NT + c * CT), lo);
+        float r[8], lo[8];
+        tmem_ld8(t_base + (uint32_t)(c * CT), r);
+        tmem_ld8(t_base + (uint32_t)(NT + c * CT), lo);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = r[i] + lo[i];
+        for (int i = 0; i < 8; ++i) v[i] = r[i] + lo[i];
       }
     };
     bool finish = whole;
     int c_first = cta, c_last = cta;
     if (!whole) {
       // publish this CTA's partial sum of the tile, then arrive on the tile's counter
-      // (acq_rel: releases the partial stores of all 128 threads, ordered before it by the
-      // barrier, and acquires the other contributors' if this arrival is the last)
-      // partial layout per (CTA, slot): [column / 4][row][column % 4], so the 32 lanes
-      // (consecutive rows) of a warp store or load 512 contiguous bytes per float4
+      // (acq_rel: releases the partial stores of all epilogue threads, ordered before it by
+      // the barrier, and acquires the other contributors' if this arrival is the last).
+      // Partial layout per (CTA, slot): [column / 4][row][column % 4], so the 32 lanes
+      // (consecutive rows) of a warp store or load 512 contiguous bytes per float4.
       const int slot = (geo.start(cta) >= tile * p.KB) ? 0 : 1;
       float* my_part = p.scratch + ((long long)cta * 2 + slot) * 128 * NT + row * 4;
-      for (int c = 0; c < nchunks; ++c) {
+      for (int c = cfirst; c < nchunks; c += CSTEP) {
         float v[CT];
         tmem_chunk(c, v);
         const int nlive = min(CT, live - c * CT);
@@ -355,15 +379,15 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
       if (lane == 0) mbar_arrive(&acc_empty[b]);
       c_first = geo.owner(tile * p.KB);
       c_last = geo.owner(tile * p.KB + p.KB - 1);
-      epi_bar();
+      epi_bar_n<EW>();
       if (et == 0) *es.flag = atomic_add_acq_rel(&p.counters[tile], 1u) == (unsigned)(c_last - c_first);
-      epi_bar();
+      epi_bar_n<EW>();
       finish = *es.flag != 0;
     }
     if (finish) {
       // The tile's final values, chunk by chunk: from TMEM (whole segment) or the sum of
       // every contributor's partial in k order (deterministic whatever the arrival order).
-      // The partial loads of chunk c+1 are issued before chunk c's epilogue stores.
+      // The partial loads of the warp's next chunk are issued before this chunk's stores.
       constexpr int kBatch = 4;
       float4 q[kBatch][CT / 4];
       auto issue = [&](int c, int cc0) {
@@ -392,9 +416,9 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
             v[4 * i4 + 3] += q[a][i4].w;
           }
       };
-      if (!whole) issue(0, c_first);
+      if (!whole && cfirst < nchunks) issue(cfirst, c_first);
 #pragma unroll 1
-      for (int c = 0; c < nchunks; ++c) {
+      for (int c = cfirst; c < nchunks; c += CSTEP) {
         float v[CT];
         if (whole) {
           tmem_chunk(c, v);
@@ -407,11 +431,11 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
             if (cc0 <= c_last) issue(c, cc0);
             else break;
           }
-          if (c + 1 < nchunks) issue(c + 1, c_first);
+          if (c + CSTEP < nchunks) issue(c + CSTEP, c_first);
         }
         const int nlive = min(CT, live - c * CT);
         finish_rows<EPI, CT>(p, n, tok0 + c * CT, nlive, v, es.rsm + c * CT, es.tpos + c * CT, es.trow + c * CT,
-                             lane, ew, es.sred, es.abest, es.stage + ew * 1024);
+                             lane, ew, es.sred + quad * 128 + c * CT, es.abest, wbuf);
       }
       if (whole) {
         tc_fence_before();
@@ -420,13 +444,24 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
       } else if (et == 0) {
         p.counters[tile] = 0u;
       }
+      if constexpr (EPI == kTcResidual) {
+        // the tile's partial sums of squares per token: its four lane quadrants, added as
+        // ((2 + 3) + (0 + 1)), for the next projection's RMSNorm
+        if (p.ss_out) {
+          epi_bar_n<EW>();
+          if (et < live)
+            p.ss_out[(long long)mt * p.ss_ld + tok0 + et] =
+                (es.sred[2 * 128 + et] + es.sred[3 * 128 + et]) + (es.sred[et] + es.sred[128 + et]);
+          epi_bar_n<EW>();
+        }
+      }
       on_tile(et);
     }
     u += len;
   }
   if constexpr (EPI == kTcLogits) {
     // one atomic per head token per CTA (a logits range covers a single token tile)
-    epi_bar();
+    epi_bar_n<EW>();
     if (ew == 0) {
       for (int i = lane; i < NT; i += 32) {
         const int t = p.ntile0 * NT + i;
@@ -435,7 +470,7 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
           atomicMax(&p.argmax[(t - p.head_lo) / p.head_stride], k);
       }
     }
-    epi_bar();
+    epi_bar_n<EW>();
   }
 }
 

@@ -37,7 +37,7 @@ namespace {
 using namespace tc;
 
 template <int EPI>
-__global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const TcParams p) {
+__global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -66,8 +66,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const TcParams p) 
     }
     mbar_init(&acc_full[0], 1);
     mbar_init(&acc_full[1], 1);
-    mbar_init(&acc_empty[0], 4);
-    mbar_init(&acc_empty[1], 4);
+    mbar_init(&acc_empty[0], kProjEpiWarps);  // one arrival per epilogue warp
+    mbar_init(&acc_empty[1], kProjEpiWarps);
     fence_barrier_init();
   }
   if (threadIdx.x < 128) es.abest[threadIdx.x] = 0ull;
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const TcParams p) 
     grid_dep_wait();
     grid_dep_launch();
     int seg = 0;
-    epilogue_range<EPI>(p, geo, blockIdx.x, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
+    epilogue_range<EPI, kProjEpiWarps>(p, geo, blockIdx.x, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
                         [](int) {});
   }
 
@@ -219,7 +219,7 @@ cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, boo
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(kProjThreads, 1, 1);
   cfg.dynamicSmemBytes = tc_proj_smem(p.NT, p.stages);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
