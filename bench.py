@@ -296,9 +296,9 @@ def kernel_roofline(model, M: int, pk: dict) -> dict:
     through the 24 layers' distinct weights (418 MB > L2), CUDA events on its stream."""
     import ctypes as C
     from qweninfer_b200 import _lib
-    from qweninfer_b200.models.qwen2 import token_tile
+    from qweninfer_b200.models.qwen2 import gate_up_tile
     dev = model.device
-    NT = token_tile(M)
+    NT = gate_up_tile(M)
     Mp = -(-M // NT) * NT
     L = _lib.lib()
     s = _lib.stream_ptr(dev)

@@ -186,6 +186,29 @@ inline int token_tile(int M) {
   return nt < cap ? nt : cap;
 }
 
+// Token tiles of the forward's projections over M tokens: {qkv, o, gate/up, down} (the
+// head's is chosen from its token range). Each epilogue writes its activation tiles in
+// the token tile of the projection that reads them, so the tiles may differ. Gate/up has
+// 76 output row tiles, enough to occupy the SMs without splitting tokens, and every
+// further token tile re-streams its 17 MB of weights: 8 up to 8 tokens, 32 up to 32, 64
+// up to 384, 128 beyond (measured on decode batches 1-128 and prefills of 32-512
+// tokens). The others take token_tile(M). QI_TILES="a,b,c,d" (powers of two 8..128, 0 =
+// the rule) overrides them for tuning.
+void token_tiles(int M, int nt[4]) {
+  static int env[4] = {-1, 0, 0, 0};
+  if (env[0] < 0) {
+    env[0] = 0;
+    if (const char* e = getenv("QI_TILES")) {
+      if (sscanf(e, "%d,%d,%d,%d", &env[0], &env[1], &env[2], &env[3]) != 4) env[0] = env[1] = env[2] = env[3] = 0;
+      for (int i = 0; i < 4; ++i)
+        if (env[i] != 0 && bad_nt(env[i])) env[i] = 0;
+    }
+  }
+  const int t = token_tile(M);
+  const int gu = M <= 8 ? 8 : M <= 32 ? 32 : M <= 384 ? 64 : 128;
+  for (int i = 0; i < 4; ++i) nt[i] = env[i] ? env[i] : (i == 2 ? gu : t);
+}
+
 // Token tile of the persistent forward: one tile covers all M <= 128 tokens (the power of
 // two >= M, at least 8); its stage table has a single token tile per projection.
 inline int persist_tile(int M) {
@@ -244,6 +267,9 @@ int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* c
   while (cols < (uint32_t)(4 * p.NT)) cols <<= 1;
   p.lg_nt = 0;
   while ((1 << p.lg_nt) < p.NT) ++p.lg_nt;
+  if (p.out_nt == 0) p.out_nt = p.NT;
+  p.lg_out_nt = 0;
+  while ((1 << p.lg_out_nt) < p.out_nt) ++p.lg_out_nt;
   p.scratch = scratch;
   p.counters = counters;
   p.stages = stages;
@@ -269,34 +295,50 @@ int grid_for(int n_tiles, int KB, int max_contrib) {
 int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
                const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
                void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots, cudaStream_t s) {
-  const int NT = token_tile(M);
-  const int n_nt = (M + NT - 1) / NT;
-  if (n_nt * NT > ws->ss_ld || !ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss || !ws->tc_scratch ||
-      !ws->tc_counters)
+  int tiles[5];
+  token_tiles(M, tiles);
+  const int NT = tiles[0];
+  for (int i = 0; i < 4; ++i)
+    if ((M + tiles[i] - 1) / tiles[i] * tiles[i] > ws->ss_ld) return QI_ERR_ARG;
+  // head token tile: the smallest (from the qkv tile up to 128) that holds all head tokens
+  // in one tile, so that the 272 MB head weights are streamed once per forward
+  const int head_hi = n_head > 0 ? head_lo + (n_head - 1) * head_stride + 1 : 0;
+  tiles[4] = NT;
+  while (n_head > 0 && tiles[4] < 128 && head_lo / tiles[4] != (head_hi - 1) / tiles[4] &&
+         (M + 2 * tiles[4] - 1) / (2 * tiles[4]) * (2 * tiles[4]) <= ws->ss_ld)
+    tiles[4] <<= 1;
+  if (!ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss || !ws->tc_scratch || !ws->tc_counters)
     return QI_ERR_ARG;
   const bool pdl = true;
   int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, slots, n_head, s, false, model->layers[0].ln1, NT,
                           ws->act_x, ws->ss, ws->ss_ld));
   if (r != QI_OK) return r;
   TcParams base = {};
-  base.NT = NT;
-  base.n_ntiles = n_nt;
   base.M = M;
   base.ss_ld = ws->ss_ld;
   base.eps = model->eps;
   base.err = ws->err;
-  auto launch = [&](TcParams& p, int max_contrib) {
-    const int g = grid_for(p.n_mtiles * p.n_ntiles, p.KB, max_contrib);
+  // projection j (0 qkv, 1 o, 2 gate/up, 3 down, 4 head) over token tile tiles[j],
+  // writing activation tiles of token tile out_nt
+  auto params = [&](int j, int out_nt) {
+    TcParams p = base;
+    p.NT = tiles[j];
+    p.n_ntiles = (M + p.NT - 1) / p.NT;
+    p.out_nt = out_nt;
+    return p;
+  };
+  auto launch = [&](TcParams& p, int j) {
+    int caps[5];
+    tc_caps(caps, p.NT);
+    const int g = grid_for(p.n_mtiles * p.n_ntiles, p.KB, caps[j]);
     return run_tc(p, ws->tc_scratch, ws->tc_scratch_floats, ws->tc_counters, ws->tc_counters_len, g, s, pdl);
   };
-  int caps[5];
-  tc_caps(caps, NT);
   const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
   for (int li = 0; li < model->num_layers; ++li) {
     const qi_layer& L = model->layers[li];
     uint16_t* kl = cache->k + li * layer_elems;
     uint16_t* vl = cache->v + li * layer_elems;
-    TcParams p = base;  // RMSNorm + QKV + bias + RoPE + KV append
+    TcParams p = params(0, 0);  // RMSNorm + QKV + bias + RoPE + KV append
     p.w = L.w_qkv;
     p.KB = kHidden / 64;
     p.n_mtiles = kQkvRows / 128;
@@ -313,11 +355,11 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.vc = vl;
     p.max_len = cache->max_len;
     p.cache_rows = cache->cache_rows;
-    if ((r = launch(p, caps[0])) != QI_OK) return r;
+    if ((r = launch(p, 0)) != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
-                  ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, NT, cache->cache_rows);
+                  ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, tiles[1], cache->cache_rows);
     if (r != QI_OK) return r;
-    p = base;  // o_proj + residual; emits RMSNorm(post_attention) inputs
+    p = params(1, tiles[2]);  // o_proj + residual; emits RMSNorm(post_attention) inputs
     p.w = L.w_o;
     p.KB = kHidden / 64;
     p.n_mtiles = kHidden / 128;
@@ -327,8 +369,8 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.next_norm_w = L.ln2;
     p.act_out = ws->act_x;
     p.ss_out = ws->ss;
-    if ((r = launch(p, caps[1])) != QI_OK) return r;
-    p = base;  // gate/up + SwiGLU
+    if ((r = launch(p, 1)) != QI_OK) return r;
+    p = params(2, tiles[3]);  // gate/up + SwiGLU
     p.w = L.w_gate_up;
     p.KB = kHidden / 64;
     p.n_mtiles = kGateUpRows / 128;
@@ -336,8 +378,8 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.ss_in = ws->ss;
     p.epi = kTcSwiglu;
     p.act_out = ws->act_h;
-    if ((r = launch(p, caps[2])) != QI_OK) return r;
-    p = base;  // down + residual; emits the next norm's inputs
+    if ((r = launch(p, 2)) != QI_OK) return r;
+    p = params(3, tiles[li + 1 < model->num_layers ? 0 : 4]);  // down + residual; emits the next norm's inputs
     p.w = L.w_down;
     p.KB = kInter / 64;
     p.n_mtiles = kHidden / 128;
@@ -347,12 +389,11 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.next_norm_w = li + 1 < model->num_layers ? model->layers[li + 1].ln1 : model->norm;
     p.act_out = ws->act_x;
     p.ss_out = ws->ss;
-    if ((r = launch(p, caps[3])) != QI_OK) return r;
+    if ((r = launch(p, 3)) != QI_OK) return r;
   }
   if (n_head > 0) {
-    const int head_hi = head_lo + (n_head - 1) * head_stride + 1;
-    for (int nt = head_lo / NT; nt <= (head_hi - 1) / NT; ++nt) {
-      TcParams p = base;  // final RMSNorm + tied head + argmax, one token tile per launch
+    for (int nt = head_lo / tiles[4]; nt <= (head_hi - 1) / tiles[4]; ++nt) {
+      TcParams p = params(4, 0);  // final RMSNorm + tied head + argmax, one token tile per launch
       p.w = model->embed;
       p.KB = kHidden / 64;
       p.n_mtiles = model->vocab / 128;
@@ -368,7 +409,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
       p.head_lo = head_lo;
       p.head_hi = head_hi;
       p.head_stride = head_stride;
-      if ((r = launch(p, caps[4])) != QI_OK) return r;
+      if ((r = launch(p, 4)) != QI_OK) return r;
     }
   }
   return QI_OK;
@@ -391,6 +432,8 @@ int plan_persistent(const qi_model* model, const qi_cache* cache, const qi_works
   TcParams base = {};
   base.NT = NT;
   base.lg_nt = lg;
+  base.out_nt = NT;
+  base.lg_out_nt = lg;
   base.n_ntiles = 1;
   base.M = M;
   base.ss_ld = ws->ss_ld;

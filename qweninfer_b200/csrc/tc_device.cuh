@@ -217,7 +217,7 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
       const float up = __shfl_xor_sync(0xffffffffu, x, 1);
       h[i] = __fdividef(x, 1.0f + __expf(-x)) * up;
     }
-    act_store_warp<CT, 1>(p.act_out, kInter, p.NT, p.lg_nt, (n - lane) >> 1, tbase, nlive, h, wbuf, lane);
+    act_store_warp<CT, 1>(p.act_out, kInter, p.out_nt, p.lg_out_nt, (n - lane) >> 1, tbase, nlive, h, wbuf, lane);
   } else if constexpr (EPI == kTcResidual) {
     // residual add into the fp32 stream (qwen2.py:237-239), then the next projection's
     // activations hi/lo(w_next * x) and this tile's partial sums of squares of x
@@ -238,7 +238,7 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
       const float s = warp_sum(xv * xv);
       if (lane == 0) sred[i] = s;  // this lane quadrant's partial of token tbase + i
     }
-    if (p.act_out) act_store_warp<CT, 0>(p.act_out, kHidden, p.NT, p.lg_nt, n - lane, tbase, nlive, an, wbuf, lane);
+    if (p.act_out) act_store_warp<CT, 0>(p.act_out, kHidden, p.out_nt, p.lg_out_nt, n - lane, tbase, nlive, an, wbuf, lane);
   } else {  // kTcLogits: tied head (qwen2.py:282-292) + greedy argmax (engine.py:155)
     // the chunk's tokens reduce as independent butterflies (one chain per token would
     // serialise 16 x 5 dependent shuffle pairs); a token counts only if it is a live

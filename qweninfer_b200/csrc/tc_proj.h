@@ -59,6 +59,8 @@ struct TcParams {
   const float* next_norm_w;
   float* ss_out;
   uint16_t* act_out;
+  int out_nt;      // token tile of act_out (the consumer's; run_tc sets 0 to NT)
+  int lg_out_nt;   // log2(out_nt)
   // logits: head tokens t = head_lo + i * head_stride (i < ...), t < head_hi
   void* logits;
   int logits_bf16;

@@ -293,6 +293,12 @@ def token_tile(M: int) -> int:
     return 8 if M <= 8 else 16 if M <= 96 else 32 if M <= 384 else 64
 
 
+def gate_up_tile(M: int) -> int:
+    """Token tile of the forward's gate/up projection for M tokens (token_tiles in
+    csrc/api.cu): 8 up to 8 tokens, 32 up to 32, 64 up to 384, 128 beyond."""
+    return 8 if M <= 8 else 32 if M <= 32 else 64 if M <= 384 else 128
+
+
 def use_persistent(M: int) -> bool:
     """Whole forward as one cooperative launch for M <= 128 tokens on the tensor-core
     path (QI_PERSISTENT=1). Off by default: its per-stage dependency chain is the same as
@@ -358,9 +364,10 @@ class Workspace:
         self.attn_part = torch.empty(parts, **f32)
         self.attn_counters = torch.zeros(max_tokens * 2, dtype=torch.int32, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
-        # tensor-core path: activation tiles (hi/lo bf16), sums of squares, stream-K scratch
-        # sized for the forward's token tile and for the persistent forward's single tile
-        nt = max(token_tile(max_tokens), 8 if max_tokens <= 8 else min(128, 1 << (max_tokens - 1).bit_length()))
+        # tensor-core path: activation tiles (hi/lo bf16), sums of squares, stream-K scratch,
+        # padded to whole 128-token tiles so that any projection's token tile (a power of
+        # two up to 128, tiles chosen per projection) and the persistent forward's fit
+        nt = 128
         pad = -(-max_tokens // nt) * nt
         bf = dict(dtype=torch.bfloat16, device=device)
         self.act_x = torch.zeros(pad * HIDDEN * 2, **bf)

@@ -274,6 +274,7 @@ def test_prefill_many_matches_single_prefills(gpu_model):
     for a, b in ((caches[0].k, caches[1].k), (caches[0].v, caches[1].v)):
         a, b = a.float().flatten(1), b.float().flatten(1)  # (layer, everything else)
         # per layer, relative to its largest value: fp32 reassociation drift (as for the
-        # hidden states) plus bf16 rounding; a misplaced token would be O(1)
+        # hidden states) plus one bf16 rounding flip (one ulp is up to 2^-7 of the value);
+        # a misplaced token would be O(1)
         err = (a - b).abs().amax(dim=1) / a.abs().amax(dim=1).clamp_min(1e-6)
-        assert bool((err <= HIDDEN_RTOL + 2 ** -8).all()), err.max().item()
+        assert bool((err <= HIDDEN_RTOL + 2 ** -7).all()), err.max().item()

@@ -40,7 +40,8 @@ def _close(ref, got):
     for a, b in ((ref[1], got[1]), (ref[2], got[2])):
         a, b = a.float().flatten(1), b.float().flatten(1)
         err = (a - b).abs().amax(dim=1) / a.abs().amax(dim=1).clamp_min(1e-6)
-        assert bool((err <= 3e-3 + 2 ** -8).all()), err.max().item()
+        # fp32 drift plus one bf16 rounding flip (one ulp is up to 2^-7 of the value)
+        assert bool((err <= 3e-3 + 2 ** -7).all()), err.max().item()
 
 
 @pytest.mark.parametrize("M", [1, 6, 16, 22, 64, 128])
