@@ -11,6 +11,7 @@
 #include "tc_proj.h"
 #include "persistent.h"
 
+#include <map>
 #include <vector>
 
 using namespace qi;
@@ -247,6 +248,41 @@ void tc_caps(int caps[5], int NT) {
   for (int i = 0; i < 5; ++i) caps[i] = env[0] > 0 ? (env[i] > 0 ? env[i] : 1) : (NT <= 32 ? small[i] : large[i]);
 }
 
+// How many projections ahead each projection of the forward prefetches weights into L2
+// (0: none). QI_L2_PF overrides it for tuning experiments.
+int l2_pf_distance() {
+  static int d = -1;
+  if (d < 0) {
+    const char* e = getenv("QI_L2_PF");
+    const int v = e ? atoi(e) : 0;
+    d = (v >= 0 && v <= 8) ? v : 0;
+  }
+  return d;
+}
+
+// Split tiles of the per-stage projections on thread-block clusters (QI_TC_CLUSTER=0
+// turns it off for tuning experiments: stream-K with global partials for every split).
+bool use_tc_clusters() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("QI_TC_CLUSTER");
+    on = (e && atoi(e) == 0) ? 0 : 1;
+  }
+  return on != 0;
+}
+
+// How many clusters of C projection CTAs with this shared memory can be resident at once
+// (cached per configuration).
+int max_clusters(int epi, int NT, int stages, int C) {
+  static std::map<long long, int> known;
+  const long long key = (((long long)epi * 256 + NT) * 64 + stages) * 16 + C;
+  auto it = known.find(key);
+  if (it != known.end()) return it->second;
+  const int n = tc_proj_max_clusters(epi, NT, stages, C);
+  known[key] = n;
+  return n;
+}
+
 // Plan and launch one tensor-core projection: grid = min(SMs, units, scratch capacity),
 // pipeline stages within the shared-memory budget, TMEM for two accumulators.
 int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* counters, int counters_len,
@@ -263,6 +299,29 @@ int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* c
   const size_t stage = 16384 + (size_t)p.NT * 256;
   int stages = (int)((size_t)tc_smem_budget_kb() * 1024 / stage);
   stages = stages < 2 ? 2 : (stages > 12 ? 12 : stages);
+  // Split tiles on thread-block clusters when every tile has the same number C (2..8) of
+  // contributors: the partials then travel through distributed shared memory instead of a
+  // global round trip and a counter. The receive buffer comes out of the ring's budget.
+  // Only in one wave: the clusters of all tiles resident at once (a cluster's CTAs share a
+  // GPC, so fewer CTAs per tile may fit where the stream-K grid would not).
+  p.cluster = 0;
+  const long long tiles = (long long)p.n_mtiles * p.n_ntiles;
+  if (use_tc_clusters() && p.epi != kTcLogits && g >= 2 * tiles) {
+    int C = (int)(g / tiles);
+    if (C > 8) C = 8;
+    if (C > p.KB) C = p.KB;
+    for (; C >= 2; --C) {
+      const size_t room = 227 * 1024 - tc_proj_smem(p.NT, 0, C);
+      int st = (int)(room / (stage + 16));
+      if (st > stages) st = stages;
+      if (st >= 2 && tiles <= max_clusters(p.epi, p.NT, st, C)) {
+        p.cluster = C;
+        stages = st;
+        g = (int)(tiles * C);
+        break;
+      }
+    }
+  }
   uint32_t cols = 32;
   while (cols < (uint32_t)(4 * p.NT)) cols <<= 1;
   p.lg_nt = 0;
@@ -327,6 +386,18 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.out_nt = out_nt;
     return p;
   };
+  // L2 prefetch: projection i of the forward's sequence (4 per layer) prefetches the
+  // weights of projection i + l2_pf_distance()
+  auto prefetch = [&](TcParams& p, int i) {
+    const int d = l2_pf_distance(), t = i + d;
+    if (d <= 0 || t >= 4 * model->num_layers) return;
+    const qi_layer& L = model->layers[t / 4];
+    const uint16_t* w[4] = {L.w_qkv, L.w_o, L.w_gate_up, L.w_down};
+    const long long rows[4] = {kQkvRows, kHidden, kGateUpRows, kHidden};
+    const long long K[4] = {kHidden, kHidden, kHidden, kInter};
+    p.pf = w[t % 4];
+    p.pf_bytes = rows[t % 4] * K[t % 4] * 2;
+  };
   auto launch = [&](TcParams& p, int j) {
     int caps[5];
     tc_caps(caps, p.NT);
@@ -355,6 +426,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.vc = vl;
     p.max_len = cache->max_len;
     p.cache_rows = cache->cache_rows;
+    prefetch(p, 4 * li);
     if ((r = launch(p, 0)) != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
                   ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, tiles[1], cache->cache_rows);
@@ -369,6 +441,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.next_norm_w = L.ln2;
     p.act_out = ws->act_x;
     p.ss_out = ws->ss;
+    prefetch(p, 4 * li + 1);
     if ((r = launch(p, 1)) != QI_OK) return r;
     p = params(2, tiles[3]);  // gate/up + SwiGLU
     p.w = L.w_gate_up;
@@ -378,6 +451,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.ss_in = ws->ss;
     p.epi = kTcSwiglu;
     p.act_out = ws->act_h;
+    prefetch(p, 4 * li + 2);
     if ((r = launch(p, 2)) != QI_OK) return r;
     p = params(3, tiles[li + 1 < model->num_layers ? 0 : 4]);  // down + residual; emits the next norm's inputs
     p.w = L.w_down;
@@ -389,6 +463,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     p.next_norm_w = li + 1 < model->num_layers ? model->layers[li + 1].ln1 : model->norm;
     p.act_out = ws->act_x;
     p.ss_out = ws->ss;
+    prefetch(p, 4 * li + 3);
     if ((r = launch(p, 3)) != QI_OK) return r;
   }
   if (n_head > 0) {

@@ -107,16 +107,24 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   uses[0] += (uint32_t)((ntiles + 1) >> 1);
   uses[1] += (uint32_t)(ntiles >> 1);
   auto parity = [&](int i) { return (uint32_t)((((i & 1) ? u1s : u0s) + (uint32_t)(i >> 1)) & 1u); };
+  // Tile i's K and V rows as 8 bulk copies (4 key quarters x K/V), one per thread
+  // 0..7: the copies one thread issues are processed one after another, so a single
+  // issuing thread would serialise them.
   auto issue = [&](int i) {
     const int k0 = kbeg + i * kTile;
     const int nk = min(kTile, kend - k0);
-    const uint32_t bytes = (uint32_t)nk * kHeadDim * 2;
     const int st = i & 1;
-    mbar_arrive_expect_tx(&S.bar[st], 2 * bytes);
-    bulk_g2s(S.k[st], kg + (long long)k0 * kHeadDim, bytes, &S.bar[st]);
-    bulk_g2s(S.v[st], vg + (long long)k0 * kHeadDim, bytes, &S.bar[st]);
+    if (tid == 0) mbar_arrive_expect_tx(&S.bar[st], (uint32_t)nk * kHeadDim * 2 * 2);
+    __syncwarp(0xffu);
+    const int q = tid & 3, kq = (nk + 3) >> 2;
+    const int a = min(nk, q * kq), b = min(nk, a + kq);
+    if (b > a) {
+      const long long o = (long long)(k0 + a) * kHeadDim;
+      if (tid < 4) bulk_g2s(S.k[st] + a * kHeadDim, kg + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
+      else bulk_g2s(S.v[st] + a * kHeadDim, vg + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
+    }
   };
-  if (tid == 0) {
+  if (tid < 8) {
     issue(0);
     if (ntiles > 1) issue(1);
   }
@@ -205,7 +213,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
       __syncwarp();
     }
     sync();  // stage st fully consumed
-    if (tid == 0 && i + 2 < ntiles) issue(i + 2);
+    if (tid < 8 && i + 2 < ntiles) issue(i + 2);
   }
 
   // Merge the 4 key groups.

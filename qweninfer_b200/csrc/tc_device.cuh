@@ -105,6 +105,10 @@ struct EpiSmem {
   int* trow;                  // 128 cache rows of the current token tile
   int* flag;                  // last-contributor broadcast
   uint16_t* stage;            // 4096: per-warp staging of activation-tile stores
+  // cluster split tiles (tc_proj_kernel only): partials of ranks 1.. ((cluster - 1) x 128 x
+  // NT floats, the partial layout) and the barrier their epilogue threads arrive on
+  float* recv;
+  uint64_t* red_full;
 };
 constexpr size_t kEpiSmemBytes = 128 * 8 + 4 * 128 * 4 + 128 * 4 + 128 * 4 + 128 * 4 + 16 + 4096 * 2;
 
@@ -117,6 +121,8 @@ __device__ __forceinline__ EpiSmem carve_epi(uint8_t* base) {  // base 8-byte al
   e.trow = e.tpos + 128;
   e.flag = e.trow + 128;
   e.stage = reinterpret_cast<uint16_t*>(base + 4624);  // 16-byte aligned when base is
+  e.recv = nullptr;
+  e.red_full = nullptr;
   return e;
 }
 
@@ -159,50 +165,81 @@ __device__ __forceinline__ void act_store_warp(uint16_t* act, int K, int NT, int
   __syncwarp();
 }
 
+// Whether the K/V of a token at position ps of cache row rw can be stored. Positions
+// outside [0, max_len) and rows outside the cache are reported (QI_ERR_INDEX) and their
+// K/V store skipped; the RoPE table lookups use position 0 for them.
+__device__ __forceinline__ bool kv_slot_ok(const TcParams& p, int ps, int rw) {
+  return ps >= 0 && ps < p.max_len && rw >= 0 && (p.cache_rows == 0 || rw < p.cache_rows);
+}
+
+// Epilogue operands of one chunk that do not depend on the accumulator: loaded before the
+// accumulator wait (first chunk) or ahead of the previous chunk's stores, so that their
+// latency overlaps the MMAs and the split-tile fix-up instead of following them.
+template <int EPI, int CT>
+struct ChunkPre {};
+template <int CT>
+struct ChunkPre<kTcQkvRope, CT> {
+  float cs[CT], sn[CT], b;
+};
+template <int CT>
+struct ChunkPre<kTcResidual, CT> {
+  float xo[CT], wn;
+};
+
+// Operands of weight row n for the nlive tokens tbase.. (tpos/trow: the chunk's positions
+// and cache rows in shared memory).
+template <int EPI, int CT>
+__device__ __forceinline__ void pre_load(const TcParams& p, int n, int tbase, int nlive, const int* tpos,
+                                         const int* trow, ChunkPre<EPI, CT>& pre) {
+  if constexpr (EPI == kTcQkvRope) {
+    const int head = n >> 6, j = (n & 63) >> 1;
+    const bool rope = head < kHeads + kKvHeads;
+    pre.b = __ldg(p.bias + n);
+#pragma unroll
+    for (int i = 0; i < CT; ++i) {
+      const int ps = i < nlive ? tpos[i] : 0;
+      const int rw = i < nlive ? trow[i] : 0;
+      const long long o = (long long)(kv_slot_ok(p, ps, rw) ? ps : 0) * kHeadDim + j;
+      pre.cs[i] = rope ? __ldg(p.rope_cos + o) : 1.0f;
+      pre.sn[i] = rope ? __ldg(p.rope_sin + o) : 0.0f;
+    }
+  } else if constexpr (EPI == kTcResidual) {
+    pre.wn = p.next_norm_w ? __ldg(p.next_norm_w + n) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < CT; ++i) pre.xo[i] = __ldcg(p.x + (long long)(tbase + (i < nlive ? i : 0)) * kHidden + n);
+  }
+}
+
 // Final epilogue of weight row n (this thread) for tokens tbase .. tbase+nlive-1 (the
 // live prefix of a chunk of CT). `v` holds D with its hi and lo columns summed; rs, tpos
 // and trow are the chunk's per-token reciprocal RMS, positions and cache rows (shared
-// memory). The 32 lanes of a warp hold 32 consecutive rows. Every global load of a chunk
-// is issued before its first global store: the compiler cannot move loads across stores
-// that may alias, and one L2 round trip per token would dominate the epilogue.
+// memory), `pre` its operands from pre_load. The 32 lanes of a warp hold 32 consecutive
+// rows.
 template <int EPI, int CT>
 __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase, int nlive, const float (&v)[CT],
-                                            const float* rs, const int* tpos, const int* trow, int lane, int ew,
-                                            float* sred, unsigned long long* abest, uint16_t* wbuf) {
+                                            const float* rs, const int* tpos, const int* trow,
+                                            const ChunkPre<EPI, CT>& pre, int lane, int ew, float* sred,
+                                            unsigned long long* abest, uint16_t* wbuf) {
   if constexpr (EPI == kTcPlain) {
 #pragma unroll
     for (int i = 0; i < CT; ++i)
       if (i < nlive) p.out[(long long)(tbase + i) * p.out_ld + n] = v[i] * rs[i];
   } else if constexpr (EPI == kTcQkvRope) {
     // bias, RoPE (qwen2.py:160-171, 86-99), q out / KV append (kv_cache.py:59-60)
-    const int head = n >> 6, j = (n & 63) >> 1, half = n & 1, d = j + 32 * half;
-    const float b = __ldg(p.bias + n);
+    const int head = n >> 6, half = n & 1, d = ((n & 63) >> 1) + 32 * half;
     const bool rope = head < kHeads + kKvHeads;
     uint16_t* kvbase = head < kHeads + kKvHeads ? p.kc : p.vc;
     const int kvh = (head - kHeads) & 1;
-    // positions outside [0, max_len) or rows outside the cache are reported (QI_ERR_INDEX)
-    // and their K/V store skipped; the table lookups use position 0 for them
-    float cs[CT], sn[CT];
-    bool ok[CT];
-#pragma unroll
-    for (int i = 0; i < CT; ++i) {
-      const int ps = i < nlive ? tpos[i] : 0;
-      const int rw = i < nlive ? trow[i] : 0;
-      ok[i] = ps >= 0 && ps < p.max_len && rw >= 0 && (p.cache_rows == 0 || rw < p.cache_rows);
-      const long long o = (long long)(ok[i] ? ps : 0) * kHeadDim + j;
-      cs[i] = rope ? __ldg(p.rope_cos + o) : 1.0f;
-      sn[i] = rope ? __ldg(p.rope_sin + o) : 0.0f;
-    }
 #pragma unroll
     for (int i = 0; i < CT; ++i) {
       if (i >= nlive) break;
       const int t = tbase + i;
-      float x = v[i] * rs[i] + b;
+      float x = v[i] * rs[i] + pre.b;
       const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
-      if (rope) x = half ? (x * cs[i] + partner * sn[i]) : (x * cs[i] - partner * sn[i]);
+      if (rope) x = half ? (x * pre.cs[i] + partner * pre.sn[i]) : (x * pre.cs[i] - partner * pre.sn[i]);
       if (head < kHeads) {
         p.q[(long long)t * kHidden + head * kHeadDim + d] = x;
-      } else if (ok[i]) {
+      } else if (kv_slot_ok(p, tpos[i], trow[i])) {
         kvbase[(((long long)trow[i] * kKvHeads + kvh) * p.max_len + tpos[i]) * kHeadDim + d] = f32_to_bf16_rn(x);
       } else if (d == 0) {
         atomicExch(p.err, QI_ERR_INDEX);
@@ -221,20 +258,16 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
   } else if constexpr (EPI == kTcResidual) {
     // residual add into the fp32 stream (qwen2.py:237-239), then the next projection's
     // activations hi/lo(w_next * x) and this tile's partial sums of squares of x
-    const float wn = p.next_norm_w ? __ldg(p.next_norm_w + n) : 1.0f;
-    float xo[CT], an[CT];
+    float an[CT];
 #pragma unroll
-    for (int i = 0; i < CT; ++i) {
-      xo[i] = __ldcg(p.x + (long long)(tbase + (i < nlive ? i : 0)) * kHidden + n);
-      an[i] = 0.f;
-    }
+    for (int i = 0; i < CT; ++i) an[i] = 0.f;
 #pragma unroll
     for (int i = 0; i < CT; ++i) {
       if (i >= nlive) break;
       const int t = tbase + i;
-      const float xv = xo[i] + v[i];
+      const float xv = pre.xo[i] + v[i];
       p.x[(long long)t * kHidden + n] = xv;
-      an[i] = xv * wn;
+      an[i] = xv * pre.wn;
       const float s = warp_sum(xv * xv);
       if (lane == 0) sred[i] = s;  // this lane quadrant's partial of token tbase + i
     }
@@ -327,10 +360,14 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
       epi_bar_n<EW>();
     }
     const int b = seg & 1;
+    const int nchunks = (min(NT, live) + CT - 1) / CT;
+    ChunkPre<EPI, CT> pre;
+    if (cfirst < nchunks)
+      pre_load<EPI, CT>(p, n, tok0 + cfirst * CT, min(CT, live - cfirst * CT), es.tpos + cfirst * CT,
+                        es.trow + cfirst * CT, pre);
     mbar_wait(&acc_full[b], (uint32_t)((seg >> 1) & 1), p.err);
     tc_fence_after();
     const uint32_t t_base = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(b * N);
-    const int nchunks = (min(NT, live) + CT - 1) / CT;
     // accumulator chunk c (columns c*CT..) with its hi and lo halves summed
     auto tmem_chunk = [&](int c, float (&v)[CT]) {
       if constexpr (CT == 16) {
@@ -358,7 +395,28 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
     };
     bool finish = whole;
     int c_first = cta, c_last = cta;
-    if (!whole) {
+    const bool clustered = !whole && p.cluster > 1;
+    if (clustered) {
+      // One cluster per tile: ranks 1.. push their partials into rank 0's receive buffer
+      // (distributed shared memory, the partial layout) and arrive on its barrier with
+      // release semantics; rank 0 finishes the tile.
+      const uint32_t rank = cluster_rank();
+      if (rank != 0) {
+        const uint32_t dst = map_rank(es.recv + (rank - 1) * 128 * NT + row * 4, 0);
+        for (int c = cfirst; c < nchunks; c += CSTEP) {
+          float v[CT];
+          tmem_chunk(c, v);
+          const int nlive = min(CT, live - c * CT);
+          for (int i = 0; i < nlive; i += 4)
+            st_cluster_v4(dst + (uint32_t)(((c * CT + i) >> 2) * 512 * 4), v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+        mbar_arrive_remote(map_rank(es.red_full, 0));
+      }
+      finish = rank == 0;
+    } else if (!whole) {
       // publish this CTA's partial sum of the tile, then arrive on the tile's counter
       // (acq_rel: releases the partial stores of all epilogue threads, ordered before it by
       // the barrier, and acquires the other contributors' if this arrival is the last).
@@ -416,12 +474,29 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
             v[4 * i4 + 3] += q[a][i4].w;
           }
       };
-      if (!whole && cfirst < nchunks) issue(cfirst, c_first);
+      if (clustered) mbar_wait_cluster(es.red_full, 0, p.err);  // every rank's partial is in
+      if (!whole && !clustered && cfirst < nchunks) issue(cfirst, c_first);
 #pragma unroll 1
       for (int c = cfirst; c < nchunks; c += CSTEP) {
         float v[CT];
         if (whole) {
           tmem_chunk(c, v);
+        } else if (clustered) {
+          // rank 0's own partial (the first k range), then ranks 1.. in order
+          tmem_chunk(c, v);
+          const int nlive = min(CT, live - c * CT);
+          for (int r = 1; r < p.cluster; ++r) {
+            const float* src = es.recv + (r - 1) * 128 * NT + row * 4 + ((c * CT) >> 2) * 512;
+#pragma unroll
+            for (int i4 = 0; i4 < CT / 4; ++i4)
+              if (4 * i4 < nlive) {
+                const float4 q4 = *reinterpret_cast<const float4*>(src + i4 * 512);
+                v[4 * i4] += q4.x;
+                v[4 * i4 + 1] += q4.y;
+                v[4 * i4 + 2] += q4.z;
+                v[4 * i4 + 3] += q4.w;
+              }
+          }
         } else {
 #pragma unroll
           for (int i = 0; i < CT; ++i) v[i] = 0.f;
@@ -433,11 +508,16 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
           }
           if (c + CSTEP < nchunks) issue(c + CSTEP, c_first);
         }
+        ChunkPre<EPI, CT> nxt;
+        const int cn = c + CSTEP;
+        if (cn < nchunks)
+          pre_load<EPI, CT>(p, n, tok0 + cn * CT, min(CT, live - cn * CT), es.tpos + cn * CT, es.trow + cn * CT, nxt);
         const int nlive = min(CT, live - c * CT);
-        finish_rows<EPI, CT>(p, n, tok0 + c * CT, nlive, v, es.rsm + c * CT, es.tpos + c * CT, es.trow + c * CT,
+        finish_rows<EPI, CT>(p, n, tok0 + c * CT, nlive, v, es.rsm + c * CT, es.tpos + c * CT, es.trow + c * CT, pre,
                              lane, ew, es.sred + quad * 128 + c * CT, es.abest, wbuf);
+        pre = nxt;
       }
-      if (whole) {
+      if (whole || clustered) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[b]);

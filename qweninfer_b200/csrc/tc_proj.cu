@@ -52,11 +52,25 @@ __global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;      // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  const EpiSmem es = carve_epi(reinterpret_cast<uint8_t*>(tmem_slot + 4));
+  uint64_t* red_full = acc_empty + 2;  // [1], cluster split tiles
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_full + 2);
+  EpiSmem es = carve_epi(reinterpret_cast<uint8_t*>(tmem_slot + 4));
+  es.recv = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(tmem_slot + 4) + kEpiSmemBytes);
+  es.red_full = red_full;
 
+  // stream-K: CTA c takes units [c*U/G, (c+1)*U/G); clusters of C: cluster q takes tile q,
+  // its rank r the k blocks [r*KB/C, (r+1)*KB/C)
+  const int C = p.cluster > 1 ? p.cluster : 1;
   const Geom geo{p.n_mtiles * p.n_ntiles * p.KB, (int)gridDim.x};
-  const int u0 = geo.start(blockIdx.x), u1 = geo.start(blockIdx.x + 1);
+  int u0, u1;
+  if (C > 1) {
+    const int tile = blockIdx.x / C, r = blockIdx.x - tile * C;
+    u0 = tile * p.KB + r * p.KB / C;
+    u1 = tile * p.KB + (r + 1) * p.KB / C;
+  } else {
+    u0 = geo.start(blockIdx.x);
+    u1 = geo.start(blockIdx.x + 1);
+  }
   const int nunits = u1 - u0;
 
   if (threadIdx.x == 0) {
@@ -68,6 +82,7 @@ __global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams
     mbar_init(&acc_full[1], 1);
     mbar_init(&acc_empty[0], kProjEpiWarps);  // one arrival per epilogue warp
     mbar_init(&acc_empty[1], kProjEpiWarps);
+    mbar_init(red_full, (uint32_t)((C - 1) * 32 * kProjEpiWarps));  // every epilogue thread of ranks 1..
     fence_barrier_init();
   }
   if (threadIdx.x < 128) es.abest[threadIdx.x] = 0ull;
@@ -79,10 +94,19 @@ __global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the barrier initialisations are visible to the whole cluster before any remote arrival:
+  // every thread arrives here and waits before its first remote access (epilogue) or
+  // before it ends (producer, MMA)
+  if (C > 1) cluster_arrive();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
-    if (lane == 0) {
+    if (lane < S) {
+      // Lane s owns ring stage s and streams the CTA's units i = s, s + S, ..: the bulk
+      // copies issued by one thread are processed one after another (~23 GB/s per thread
+      // for 16 KB copies), so one issuing lane per stage keeps S copies in flight.
+      const int s = lane;
+      uint8_t* st = stage_base + (size_t)s * stage_bytes;
       auto src_a = [&](int u) {
         const int tile = u / p.KB, kb = u - tile * p.KB;
         return p.w + ((long long)(tile / p.n_ntiles) * p.KB + kb) * (kABytes / 2);
@@ -92,27 +116,31 @@ __global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams
         const int nt = tile % p.n_ntiles + p.ntile0;
         return p.act_in + ((long long)nt * p.KB + kb) * (b_bytes / 2);
       };
-      const int pre = nunits < S ? nunits : S;
-      for (int i = 0; i < pre; ++i) {  // weights only: they do not depend on earlier kernels
-        mbar_arrive_expect_tx(&full[i], stage_bytes);
-        bulk_g2s(stage_base + (size_t)i * stage_bytes, src_a(u0 + i), kABytes, &full[i]);
+      if (s < nunits) {  // weights only: they do not depend on earlier kernels
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        bulk_g2s(st, src_a(u0 + s), kABytes, &full[s]);
       }
       grid_dep_wait();
-      for (int i = 0; i < pre; ++i)
-        bulk_g2s(stage_base + (size_t)i * stage_bytes + kABytes, src_b(u0 + i), b_bytes, &full[i]);
-      for (int i = pre; i < nunits; ++i) {
-        const int s = i % S;
+      if (s < nunits) bulk_g2s(st + kABytes, src_b(u0 + s), b_bytes, &full[s]);
+      for (int i = s + S; i < nunits; i += S) {
         mbar_wait(&empty[s], (uint32_t)(((i / S) & 1) ^ 1), p.err);
-        uint8_t* st = stage_base + (size_t)s * stage_bytes;
         mbar_arrive_expect_tx(&full[s], stage_bytes);
         bulk_g2s(st, src_a(u0 + i), kABytes, &full[s]);
         bulk_g2s(st + kABytes, src_b(u0 + i), b_bytes, &full[s]);
       }
     } else {
+      if (lane == 31 && p.pf_bytes > 0) {
+        // this CTA's contiguous share of a later projection's weights, in 16 KB blocks;
+        // independent of earlier kernels, so issued before the programmatic-launch wait
+        const long long nblk = p.pf_bytes / kABytes, per = (nblk + gridDim.x - 1) / gridDim.x;
+        const long long b1 = min(nblk, (blockIdx.x + 1) * per);
+        for (long long b = blockIdx.x * per; b < b1; ++b) bulk_prefetch_l2(p.pf + b * (kABytes / 2), kABytes);
+      }
       grid_dep_wait();
     }
     grid_dep_launch();
     __syncwarp();
+    if (C > 1) cluster_wait();
   } else if (warp == 1) {
     // --------------------------------------------------------------------- MMA
     grid_dep_wait();
@@ -144,10 +172,12 @@ __global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams
       }
     }
     __syncwarp();
+    if (C > 1) cluster_wait();
   } else {
     // ---------------------------------------------------------------- epilogue
     grid_dep_wait();
     grid_dep_launch();
+    if (C > 1) cluster_wait();
     int seg = 0;
     epilogue_range<EPI, kProjEpiWarps>(p, geo, blockIdx.x, u0, u1, seg, acc_full, acc_empty, tmem_base, N, warp, lane, es,
                         [](int) {});
@@ -196,9 +226,10 @@ __global__ void __launch_bounds__(256) act_tiles_kernel(const float* __restrict_
 
 }  // namespace
 
-size_t tc_proj_smem(int NT, int stages) {
+size_t tc_proj_smem(int NT, int stages, int cluster) {
   const size_t stage_bytes = kABytes + (size_t)NT * 256;
-  return (size_t)stages * stage_bytes + (size_t)stages * 16 + 32 + 16 + kEpiSmemBytes;
+  const size_t recv = cluster > 1 ? (size_t)(cluster - 1) * 128 * NT * 4 : 0;
+  return (size_t)stages * stage_bytes + (size_t)stages * 16 + 48 + 16 + kEpiSmemBytes + recv;
 }
 
 cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, bool pdl) {
@@ -220,14 +251,50 @@ cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, boo
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas, 1, 1);
   cfg.blockDim = dim3(kProjThreads, 1, 1);
-  cfg.dynamicSmemBytes = tc_proj_smem(p.NT, p.stages);
+  cfg.dynamicSmemBytes = tc_proj_smem(p.NT, p.stages, p.cluster);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n++].val.programmaticStreamSerializationAllowed = 1;
+  }
+  if (p.cluster > 1) {
+    if (ctas % p.cluster != 0 || p.cluster > 8) return cudaErrorInvalidValue;
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)p.cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n++].val.clusterDim.z = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+int tc_proj_max_clusters(int epi, int NT, int stages, int cluster) {
+  void (*kern)(TcParams) = epi == kTcQkvRope    ? tc_proj_kernel<kTcQkvRope>
+                           : epi == kTcResidual ? tc_proj_kernel<kTcResidual>
+                           : epi == kTcSwiglu   ? tc_proj_kernel<kTcSwiglu>
+                           : epi == kTcLogits   ? tc_proj_kernel<kTcLogits>
+                                                : tc_proj_kernel<kTcPlain>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster, 1, 1);
+  cfg.blockDim = dim3(kProjThreads, 1, 1);
+  cfg.dynamicSmemBytes = tc_proj_smem(NT, stages, cluster);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
 }
 
 cudaError_t launch_act_tiles(const float* x, const float* norm_w, int M, int K, int NT, uint16_t* act, float* ss,

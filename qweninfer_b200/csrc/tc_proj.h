@@ -67,7 +67,13 @@ struct TcParams {
   long long logits_ld;
   unsigned long long* argmax;
   int head_lo, head_hi, head_stride;
-  // stream-K
+  // L2 prefetch: bytes from pf (a later projection's weights) spread over the CTAs
+  const uint16_t* pf;
+  long long pf_bytes;      // multiple of 16 KB, or 0
+  // split tiles: cluster > 1 runs each output tile on one thread-block cluster of that
+  // many CTAs (k ranges in rank order, partials summed in the rank-0 CTA's shared memory);
+  // otherwise stream-K over the grid with partials in `scratch`
+  int cluster;
   float* scratch;          // gridDim.x * 2 * 128 * NT floats
   unsigned int* counters;  // one per (m-tile, token tile), zero between launches
   int stages;
@@ -75,8 +81,10 @@ struct TcParams {
   int* err;
 };
 
-size_t tc_proj_smem(int NT, int stages);
+size_t tc_proj_smem(int NT, int stages, int cluster);
 cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, bool pdl);
+// clusters of `cluster` tc_proj CTAs that can be resident at once (0: none, or an error)
+int tc_proj_max_clusters(int epi, int NT, int stages, int cluster);
 
 // x (M, K) fp32 -> activation tiles of (norm_w * x) (norm_w may be null) and, if ss is
 // non-null, per-token sums of squares of x in ss[0][t] (ss[1..6][t] = 0; K must be 896).
