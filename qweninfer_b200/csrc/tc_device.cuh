@@ -230,19 +230,24 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
     const bool rope = head < kHeads + kKvHeads;
     uint16_t* kvbase = head < kHeads + kKvHeads ? p.kc : p.vc;
     const int kvh = (head - kHeads) & 1;
+    // the chunk's tokens as independent chains (no early exit: predicated stores)
+    float x[CT], partner[CT];
+#pragma unroll
+    for (int i = 0; i < CT; ++i) x[i] = v[i] * rs[i] + pre.b;
+#pragma unroll
+    for (int i = 0; i < CT; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, x[i], 1);
 #pragma unroll
     for (int i = 0; i < CT; ++i) {
-      if (i >= nlive) break;
-      const int t = tbase + i;
-      float x = v[i] * rs[i] + pre.b;
-      const float partner = __shfl_xor_sync(0xffffffffu, x, 1);
-      if (rope) x = half ? (x * pre.cs[i] + partner * pre.sn[i]) : (x * pre.cs[i] - partner * pre.sn[i]);
-      if (head < kHeads) {
-        p.q[(long long)t * kHidden + head * kHeadDim + d] = x;
-      } else if (kv_slot_ok(p, tpos[i], trow[i])) {
-        kvbase[(((long long)trow[i] * kKvHeads + kvh) * p.max_len + tpos[i]) * kHeadDim + d] = f32_to_bf16_rn(x);
-      } else if (d == 0) {
-        atomicExch(p.err, QI_ERR_INDEX);
+      if (rope) x[i] = half ? (x[i] * pre.cs[i] + partner[i] * pre.sn[i]) : (x[i] * pre.cs[i] - partner[i] * pre.sn[i]);
+      if (i < nlive) {
+        const int t = tbase + i;
+        if (head < kHeads) {
+          p.q[(long long)t * kHidden + head * kHeadDim + d] = x[i];
+        } else if (kv_slot_ok(p, tpos[i], trow[i])) {
+          kvbase[(((long long)trow[i] * kKvHeads + kvh) * p.max_len + tpos[i]) * kHeadDim + d] = f32_to_bf16_rn(x[i]);
+        } else if (d == 0) {
+          atomicExch(p.err, QI_ERR_INDEX);
+        }
       }
     }
   } else if constexpr (EPI == kTcSwiglu) {
@@ -258,18 +263,24 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
   } else if constexpr (EPI == kTcResidual) {
     // residual add into the fp32 stream (qwen2.py:237-239), then the next projection's
     // activations hi/lo(w_next * x) and this tile's partial sums of squares of x
-    float an[CT];
-#pragma unroll
-    for (int i = 0; i < CT; ++i) an[i] = 0.f;
+    // the chunk's tokens as independent chains: predicated stores, and the sums of squares
+    // as interleaved butterflies (each token's in the order of warp_sum)
+    float an[CT], sq[CT];
 #pragma unroll
     for (int i = 0; i < CT; ++i) {
-      if (i >= nlive) break;
-      const int t = tbase + i;
       const float xv = pre.xo[i] + v[i];
-      p.x[(long long)t * kHidden + n] = xv;
-      an[i] = xv * pre.wn;
-      const float s = warp_sum(xv * xv);
-      if (lane == 0) sred[i] = s;  // this lane quadrant's partial of token tbase + i
+      an[i] = i < nlive ? xv * pre.wn : 0.f;
+      sq[i] = xv * xv;
+      if (i < nlive) p.x[(long long)(tbase + i) * kHidden + n] = xv;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < CT; ++i) sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], o);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i < CT; ++i)
+        if (i < nlive) sred[i] = sq[i];  // this lane quadrant's partial of token tbase + i
     }
     if (p.act_out) act_store_warp<CT, 0>(p.act_out, kHidden, p.out_nt, p.lg_out_nt, n - lane, tbase, nlive, an, wbuf, lane);
   } else {  // kTcLogits: tied head (qwen2.py:282-292) + greedy argmax (engine.py:155)
@@ -304,6 +315,24 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
   }
 }
 
+// Reads the kernel parameters a projection's finish uses, so that their constant-cache
+// lines are filled while the MMAs run: a parameter's first read misses and waits about an
+// L2 round trip, which would otherwise fall after the accumulator (~1 us per tile).
+template <int EPI>
+__device__ __forceinline__ void warm_params(const TcParams& p) {
+  asm volatile("" ::"l"(p.scratch), "l"(p.counters), "r"(p.cluster), "l"(p.err), "r"(p.M), "r"(p.n_ntiles),
+               "r"(p.ntile0));
+  if constexpr (EPI == kTcPlain) asm volatile("" ::"l"(p.out), "r"(p.out_ld));
+  if constexpr (EPI == kTcQkvRope)
+    asm volatile("" ::"l"(p.q), "l"(p.kc), "l"(p.vc), "r"(p.max_len), "r"(p.cache_rows));
+  if constexpr (EPI == kTcResidual)
+    asm volatile("" ::"l"(p.x), "l"(p.act_out), "r"(p.out_nt), "r"(p.lg_out_nt), "l"(p.ss_out), "r"(p.ss_ld));
+  if constexpr (EPI == kTcSwiglu) asm volatile("" ::"l"(p.act_out), "r"(p.out_nt), "r"(p.lg_out_nt));
+  if constexpr (EPI == kTcLogits)
+    asm volatile("" ::"l"(p.logits), "r"(p.logits_bf16), "l"(p.logits_ld), "l"(p.argmax), "r"(p.head_lo),
+                 "r"(p.head_hi), "r"(p.head_stride));
+}
+
 // Epilogue of a CTA's stream-K units [u0, u1) of one projection, run by EW epilogue warps
 // (4 or 8). Warp w reads TMEM lane quadrant w % 4 (rows 32 * (w % 4) ..) and, with 8
 // warps, the token chunks c = w / 4, w / 4 + 2, .. of CT columns, so two warps share each
@@ -327,6 +356,7 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
   const int row = quad * 32 + lane;
   const int et = ew * 32 + lane;
   uint16_t* wbuf = es.stage + ew * (4096 / EW);
+  warm_params<EPI>(p);
   int cur_nt = -1;
   for (int u = u0; u < u1; ++seg) {
     const int tile = u / p.KB, kb0 = u - tile * p.KB;
