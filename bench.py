@@ -52,9 +52,9 @@ MAX_LEN = 512
 WEIGHT_BYTES = 988_065_536          # bf16 layer weights + norms + biases + tied head
 KV_BYTES_PER_TOKEN = 12_288         # 2 (K,V) * 24 layers * 2 heads * 64 * 2 B
 # DRAM bytes (read + write) per launch of tc_proj_kernel<swiglu> by token tile, from one
-# ncu capture of the same launch (profiles/tc_proj_swiglu_decode.md: token tile 16; 32 from
-# an earlier capture of the same kernel); None until captured.
-TRAFFIC: dict[int, int | None] = {16: 17_615_616, 32: 18_066_944}
+# ncu capture of the same launch (profiles/tc_proj_swiglu_decode.md: token tile 32, the
+# batch-22 case; 16 from an earlier capture of the same kernel); None until captured.
+TRAFFIC: dict[int, int | None] = {16: 17_615_616, 32: 17_612_288}
 EMBED_ROW_BYTES = 1_792
 
 
