@@ -13,18 +13,21 @@
 // producing kernel writes activations the same way (tc_proj.h), so a pipeline stage is
 // two contiguous cp.async.bulk copies.
 //
-// Work split: U = (m-tiles x token tiles x k-blocks) units; CTA c of G takes units
-// [c*U/G, (c+1)*U/G). A run of units inside one tile is a segment. A tile covered by a
-// single segment is finished straight from TMEM; a tile shared by several CTAs is
+// Work split: U = (m-tiles x token tiles x k-blocks) units. Stream-K: CTA c of G takes
+// units [c*U/G, (c+1)*U/G); a run of units inside one tile is a segment. A tile covered
+// by a single segment is finished straight from TMEM; a tile shared by several CTAs is
 // finished by the last contributor to arrive (per-tile counter), which sums the
-// contributors' fp32 partials in k order — results do not depend on timing or on how
-// many tokens are in the batch.
+// contributors' fp32 partials in k order. Clusters (TcParams::cluster = C > 1): cluster q
+// of C CTAs takes tile q, rank r the k blocks [r*KB/C, (r+1)*KB/C); ranks 1.. push their
+// partials into rank 0's shared memory (distributed shared memory) and rank 0 finishes the
+// tile, adding them in rank order. Either way the sums do not depend on timing.
 //
-// Warp roles (6 warps): warp 0 streams stages (weights may be fetched before the
-// programmatic-launch wait, activations only after it); warp 1 owns TMEM and one of its
-// threads issues the UMMAs; warps 2-5 are the epilogue (TMEM lane quadrant = warp % 4,
-// one weight row per thread). Two TMEM accumulators let the epilogue of one segment
-// overlap the UMMAs of the next. Every mbarrier wait is bounded (error word on timeout).
+// Warp roles (10 warps): warp 0 streams stages, one issuing lane per ring stage (weights
+// may be fetched before the programmatic-launch wait, activations only after it); warp 1
+// owns TMEM and one of its threads issues the UMMAs; warps 2-9 are the epilogue (TMEM lane
+// quadrant = warp % 4, one weight row per thread, the two warps of a quadrant on
+// alternate token chunks). Two TMEM accumulators let the epilogue of one segment overlap
+// the UMMAs of the next. Every mbarrier wait is bounded (error word on timeout).
 #include "common.cuh"
 #include "internal.h"
 #include "tc_proj.h"
