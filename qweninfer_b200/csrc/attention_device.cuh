@@ -78,29 +78,6 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   const uint16_t* kg = p.kc + head_base;
   const uint16_t* vg = p.vc + head_base;
 
-  // q of the 7 heads sharing KV head g, pre-scaled by 1/8 (exact), laid out so that the
-  // eight 8-dim chunks' first halves are 16-byte neighbours (conflict-free rotated reads).
-  // (all four loads of a thread are issued before its shared-memory stores)
-  {
-    constexpr int kRounds = (kGqa * kHeadDim + NT - 1) / NT;
-    float qv[kRounds];
-#pragma unroll
-    for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * NT;
-      qv[r] = __ldcg(p.q + (long long)tok * kHidden + g * kGqa * kHeadDim + (idx < kGqa * kHeadDim ? idx : 0));
-    }
-#pragma unroll
-    for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * NT;
-      if (idx < kGqa * kHeadDim) {
-        const int h = idx >> 6, d = idx & 63;
-        const int cc = d >> 3, e = d & 7;
-        S.q[((h * 2 + (e >> 2)) * 8 + cc) * 4 + (e & 3)] = qv[r] * 0.125f;
-      }
-    }
-  }
-  sync();
-
   const int ntiles = (kend - kbeg + kTile - 1) / kTile;
   // mbarrier phases continue across the units a CTA runs: tile i uses stage i & 1
   const uint32_t u0s = uses[0], u1s = uses[1];
@@ -124,10 +101,35 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
       else bulk_g2s(S.v[st] + a * kHeadDim, vg + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
     }
   };
+  // the first two tiles are requested before q is staged: the copies do not depend on
+  // it, so their latency overlaps the q loads
   if (tid < 8) {
     issue(0);
     if (ntiles > 1) issue(1);
   }
+
+  // q of the 7 heads sharing KV head g, pre-scaled by 1/8 (exact), laid out so that the
+  // eight 8-dim chunks' first halves are 16-byte neighbours (conflict-free rotated reads).
+  // (all four loads of a thread are issued before its shared-memory stores)
+  {
+    constexpr int kRounds = (kGqa * kHeadDim + NT - 1) / NT;
+    float qv[kRounds];
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int idx = tid + r * NT;
+      qv[r] = __ldcg(p.q + (long long)tok * kHidden + g * kGqa * kHeadDim + (idx < kGqa * kHeadDim ? idx : 0));
+    }
+#pragma unroll
+    for (int r = 0; r < kRounds; ++r) {
+      const int idx = tid + r * NT;
+      if (idx < kGqa * kHeadDim) {
+        const int h = idx >> 6, d = idx & 63;
+        const int cc = d >> 3, e = d & 7;
+        S.q[((h * 2 + (e >> 2)) * 8 + cc) * 4 + (e & 3)] = qv[r] * 0.125f;
+      }
+    }
+  }
+  sync();
 
   float m[HPG], l[HPG], acc[HPG][2];
 #pragma unroll
