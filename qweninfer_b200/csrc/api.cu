@@ -79,6 +79,8 @@ int qkv(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv, con
   return run_gemv(kEpiQkvRope, p, kQkvRows, kHidden, sm_count(), 8, s, pdl);
 }
 
+bool use_tc_clusters();
+
 int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int32_t* pos, const int32_t* rows,
               int M, int max_len, int split_keys, int max_splits, float* out, float* part, unsigned int* counters,
               int* err, cudaStream_t s, bool pdl, uint16_t* out_act = nullptr, int out_nt = 0,
@@ -101,6 +103,8 @@ int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int3
   a.part = part;
   a.counters = counters;
   a.err = err;
+  // splits of a token merged inside a cluster when a launch has 2..8 of them
+  a.cluster = (use_tc_clusters() && max_splits >= 2 && max_splits <= 8) ? 1 : 0;
   return rc(launch_attention(a, s, pdl));
 }
 
@@ -260,8 +264,9 @@ int l2_pf_distance() {
   return d;
 }
 
-// Split tiles of the per-stage projections on thread-block clusters (QI_TC_CLUSTER=0
-// turns it off for tuning experiments: stream-K with global partials for every split).
+// Split tiles of the per-stage projections, and attention's key splits, reduced inside
+// thread-block clusters (QI_TC_CLUSTER=0 turns it off for tuning experiments: partials
+// through global scratch and arrival counters everywhere).
 bool use_tc_clusters() {
   static int on = -1;
   if (on < 0) {

@@ -7,8 +7,10 @@
 // The 7 query heads of the KV group share every tile: 4 warps each take 32 keys of a
 // tile, compute all 7 scores per key (lane = key), run an fp32 online softmax per warp,
 // and accumulate P.V with lane = 2 output dims. Warps and splits are merged with the
-// usual max-rescaled sums; the last CTA of a token/head (atomic arrival count) merges
-// the splits in split order and resets its counter.
+// usual max-rescaled sums, in split order: with 2-8 splits per launch the splits of a
+// token/head form one thread-block cluster and merge in split 0's shared memory;
+// otherwise the last CTA of a token/head (atomic arrival count) merges them from global
+// scratch and resets its counter.
 #include <mutex>
 
 #include "common.cuh"
@@ -22,41 +24,67 @@ namespace {
 
 using namespace attn;
 
+constexpr size_t kMergeOffset = (sizeof(AttnSmem) + 15) / 16 * 16;
+
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
+  ClusterMerge* cm = p.cluster ? reinterpret_cast<ClusterMerge*>(smem_raw + kMergeOffset) : nullptr;
   grid_dep_wait();
   grid_dep_launch();
   if (threadIdx.x == 0) {
     mbar_init(&S.bar[0], 1);
     mbar_init(&S.bar[1], 1);
+    if (cm) {
+      // split 0 waits for one arrival per thread of each other split of its token
+      const int ps = p.pos[blockIdx.z];
+      const int nsplit = (ps >= 0 && ps < p.max_len) ? (ps + p.split_keys) / p.split_keys : 1;
+      mbar_init(&cm->bar, (uint32_t)(nsplit > 1 ? (nsplit - 1) * kAttnThreads : 1));
+    }
     fence_barrier_init();
   }
   __syncthreads();
+  // Cluster handshake: every thread arrives once the barriers are initialised and waits
+  // before its first remote access (the splits that push, inside the unit) or before it
+  // ends (all others), so no CTA waits for it up front.
+  if (cm) cluster_arrive();
   uint32_t uses[2] = {0u, 0u};
-  attention_unit<false, 8>(p, S, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, uses);
+  bool waited = false;
+  attention_unit<false, 8>(p, S, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, uses, cm, &waited);
+  if (cm && !waited) cluster_wait();
 }
 
 }  // namespace
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
   static bool configured = false;
-  const size_t smem = sizeof(AttnSmem);
+  const size_t smem_max = kMergeOffset + sizeof(ClusterMerge);
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
     if (e != cudaSuccess) return e;
     configured = true;
   }
+  if (p.cluster && (p.max_splits < 2 || p.max_splits > kMaxClusterSplits)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.max_splits, kKvHeads, p.M);
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = p.cluster ? smem_max : sizeof(AttnSmem);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n++].val.programmaticStreamSerializationAllowed = 1;
+  }
+  if (p.cluster) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)p.max_splits;
+    attr[n].val.clusterDim.y = 1;
+    attr[n++].val.clusterDim.z = 1;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, attention_kernel, p);
 }
 

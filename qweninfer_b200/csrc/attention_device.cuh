@@ -32,6 +32,15 @@ struct AttnSmem {
   int last;
 };
 
+// Split merge in a thread-block cluster (standalone kernel, AttnParams::cluster): the
+// partials of splits 0.. of one (token, KV head) in split 0's shared memory, and the
+// barrier that the other splits' threads arrive on once theirs is stored.
+constexpr int kMaxClusterSplits = 8;
+struct ClusterMerge {
+  float recv[kMaxClusterSplits][kPartStride];
+  uint64_t bar;
+};
+
 // Output element (token, feature f = head * 64 + d): fp32 and/or the o projection's
 // activation tiles (hi/lo bf16 halves).
 __device__ __forceinline__ void emit(const AttnParams& p, int tok, int f, float v) {
@@ -45,9 +54,13 @@ __device__ __forceinline__ void emit(const AttnParams& p, int tok, int f, float 
 
 // Runs unit (split, g, tok); returns true when it wrote the final output of (tok, g)
 // (a single split, or the last split to arrive, which merges all of them).
+// cm: the cluster merge buffer (standalone kernel with AttnParams::cluster), else null;
+// *waited is set when the unit waited on the cluster barrier (a split that pushes its
+// partial to split 0 does so before its first remote store).
 template <bool kNamedBarrier, int NW>
 __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S, int split, int g, int tok,
-                                               int tid, uint32_t (&uses)[2]) {
+                                               int tid, uint32_t (&uses)[2], ClusterMerge* cm = nullptr,
+                                               bool* waited = nullptr) {
   static_assert(NW == 4 || NW == 8, "4 or 8 warps");
   static_assert(!kNamedBarrier || NW == 4, "the named barrier spans 4 warps");
   constexpr int NT = NW * 32;
@@ -232,7 +245,16 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     }
   }
   sync();
+  // this split's partial: (A[64], m, l) per head, in global scratch, in split 0's
+  // shared memory (cluster: split 0 writes its own, the others over distributed shared
+  // memory), or straight to the output when there is a single split
   float* part = p.part + (((long long)tok * kKvHeads + g) * p.max_splits + split) * kPartStride;
+  const bool push = cm && nsplit > 1 && split > 0;
+  if (push) {
+    cluster_wait();  // split 0's barrier initialisation is visible (uniform over the CTA)
+    *waited = true;
+  }
+  const uint32_t remote = push ? map_rank(&cm->recv[split][0], 0) : 0u;
   for (int idx = tid; idx < kGqa * (kHeadDim + 2); idx += NT) {
     const int h = idx / (kHeadDim + 2);
     const int d = idx - h * (kHeadDim + 2);
@@ -248,29 +270,48 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
       L = fmaf(sc, S.cmb[w][h][kHeadDim + 1], L);
       if (d < kHeadDim) A = fmaf(sc, S.cmb[w][h][d], A);
     }
+    const float val = d < kHeadDim ? A : (d == kHeadDim ? mx : L);
     if (nsplit == 1) {
       if (d < kHeadDim) emit(p, tok, (g * kGqa + h) * kHeadDim + d, A / L);
+    } else if (!cm) {
+      part[idx] = val;
+    } else if (split == 0) {
+      cm->recv[0][idx] = val;
     } else {
-      part[idx] = d < kHeadDim ? A : (d == kHeadDim ? mx : L);
+      st_cluster_f32(remote + (uint32_t)idx * 4u, val);
     }
   }
   if (nsplit == 1) return true;
+  if (cm && split > 0) {
+    // every thread's stores are released to split 0 by its own arrival
+    mbar_arrive_remote(map_rank(&cm->bar, 0));
+    return false;
+  }
 
-  // Split merge by the last-arriving CTA of this (token, head): the barrier orders every
-  // thread's partial stores before thread 0's acq_rel arrival.
-  sync();
-  if (tid == 0) S.last = atomic_add_acq_rel(&p.counters[tok * kKvHeads + g], 1u) == (unsigned int)(nsplit - 1);
-  sync();
-  if (!S.last) return false;
+  if (cm) {
+    // split 0: its own partial is in place (barrier) and every other split's has arrived
+    sync();
+    mbar_wait_cluster(&cm->bar, 0, p.err);
+  } else {
+    // Split merge by the last-arriving CTA of this (token, head): the barrier orders every
+    // thread's partial stores before thread 0's acq_rel arrival.
+    sync();
+    if (tid == 0) S.last = atomic_add_acq_rel(&p.counters[tok * kKvHeads + g], 1u) == (unsigned int)(nsplit - 1);
+    sync();
+    if (!S.last) return false;
+  }
   const float* base = p.part + (((long long)tok * kKvHeads + g) * p.max_splits) * kPartStride;
+  // partial value `off` of split s
+  auto load = [&](int s, int off) -> float {
+    return cm ? cm->recv[s][off] : __ldcg(base + (long long)s * kPartStride + off);
+  };
   // (1) every split's running max and sum into shared memory (reusing the warp-merge
   // area: 2 * 7 * nsplit + 7 floats), (2) per head the max and the split weights
   // exp(m_s - max), (3) the weighted sum of the split outputs, loads before stores.
   float* sm = &S.cmb[0][0][0];
   for (int idx = tid; idx < kGqa * nsplit; idx += NT) {
     const int h = idx / nsplit, s = idx - h * nsplit;
-    const float* ph = base + s * kPartStride + h * (kHeadDim + 2);
-    const float mv = __ldcg(ph + kHeadDim), lv = __ldcg(ph + kHeadDim + 1);
+    const float mv = load(s, h * (kHeadDim + 2) + kHeadDim), lv = load(s, h * (kHeadDim + 2) + kHeadDim + 1);
     sm[idx] = mv;
     sm[kGqa * nsplit + idx] = lv;
   }
@@ -295,13 +336,12 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     for (int r = 0; r < kRounds; ++r) A[r] = 0.f;
 #pragma unroll 4
     for (int s = 0; s < nsplit; ++s) {
-      const float* ps = base + s * kPartStride;
 #pragma unroll
       for (int r = 0; r < kRounds; ++r) {
         const int idx = tid + r * NT;
         if (idx < kGqa * kHeadDim) {
           const int h = idx >> 6, d = idx & 63;
-          A[r] = fmaf(sm[h * nsplit + s], __ldcg(ps + h * (kHeadDim + 2) + d), A[r]);
+          A[r] = fmaf(sm[h * nsplit + s], load(s, h * (kHeadDim + 2) + d), A[r]);
         }
       }
     }
@@ -311,7 +351,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
       if (idx < kGqa * kHeadDim) emit(p, tok, g * kGqa * kHeadDim + idx, A[r] / sm[2 * kGqa * nsplit + (idx >> 6)]);
     }
   }
-  if (tid == 0) p.counters[tok * kKvHeads + g] = 0u;
+  if (!cm && tid == 0) p.counters[tok * kKvHeads + g] = 0u;
   return true;
 }
 

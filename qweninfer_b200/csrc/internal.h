@@ -71,6 +71,9 @@ struct AttnParams {
   float* part;
   unsigned int* counters;
   int* err;
+  // 1: the key splits of a (token, KV head) form one thread-block cluster of max_splits
+  // CTAs (2..8) and are merged in split 0's shared memory; 0: merged through part/counters
+  int cluster;
 };
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
