@@ -1,0 +1,48 @@
+"""Host-side launch plans of the forward (no GPU needed): attention key splits and the
+token tiles of the tensor-core projections. The kernels rely on these invariants: every
+key of a row is covered by some split, a decode launch whose splits merge inside one
+thread-block cluster has at most 8 of them, split sizes are whole 128-key tiles, and the
+token tiles never shrink as the token count grows (a workspace sized for its largest
+forward then covers every smaller one)."""
+
+from __future__ import annotations
+
+import pytest
+
+from qweninfer_b200.models.qwen2 import _split_plan, gate_up_tile, token_tile
+
+
+@pytest.mark.parametrize("max_len", [1, 96, 128, 129, 512, 1000, 1024, 1025, 2048, 4096, 32768])
+@pytest.mark.parametrize("M", [1, 22, 64, 65, 512])
+def test_split_plan_covers_every_key(M, max_len):
+    split, n = _split_plan(M, max_len)
+    assert split % 128 == 0 and split >= 128
+    assert n >= 1 and split * n >= max_len
+    assert split * (n - 1) < max_len  # no split that can never hold a key
+    assert n <= 128  # the merge's capacity
+
+
+@pytest.mark.parametrize("max_len", [96, 256, 512, 1024])
+def test_decode_splits_fit_one_cluster(max_len):
+    split, n = _split_plan(22, max_len)
+    assert split == 128 and n <= 8
+
+
+def test_prefill_splits_are_coarse():
+    assert _split_plan(512, 512) == (1024, 1)
+    assert _split_plan(65, 4096)[0] == 1024
+
+
+@pytest.mark.parametrize("rule", [token_tile, gate_up_tile])
+def test_token_tiles_non_decreasing_powers_of_two(rule):
+    prev = 0
+    for M in range(1, 2049):
+        t = rule(M)
+        assert 8 <= t <= 128 and t & (t - 1) == 0
+        assert t >= prev, M
+        prev = t
+
+
+def test_token_tile_rules():
+    assert [token_tile(M) for M in (1, 8, 9, 96, 97, 384, 385)] == [8, 8, 16, 16, 32, 32, 64]
+    assert [gate_up_tile(M) for M in (1, 8, 9, 32, 33, 384, 385)] == [8, 8, 32, 32, 64, 64, 128]
