@@ -208,8 +208,13 @@ typedef struct {
   uint16_t* act_attn;       /* same size                                      */
   uint16_t* act_h;          /* K = 4864: ss_ld * 19456 bytes                  */
   float* ss;                /* 7 * ss_ld floats: per-128-feature sums of squares */
-  int ss_ld;                /* >= tokens rounded up to the token tile          */
-  float* tc_scratch;        /* stream-K partials, >= 148*2*128*token_tile floats */
+  int ss_ld;                /* >= tokens rounded up to the token tile (8 up to 8
+                               tokens, 16 up to 96, 32 up to 384, else 64); padding
+                               to 128 lets every projection use its own, larger
+                               tile where that measured faster (the Python
+                               Workspace pads so)                                */
+  float* tc_scratch;        /* stream-K partials, 148*2*128*128 floats covers every
+                               token tile (less only lowers the CTAs of a launch) */
   long long tc_scratch_floats;
   unsigned int* tc_counters;/* one per output tile, zero-initialised          */
   int tc_counters_len;

@@ -361,6 +361,9 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
                void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots, cudaStream_t s) {
   int tiles[5];
   token_tiles(M, tiles);
+  // a workspace padded less than to 128 tokens gets the largest tiles that fit it
+  for (int i = 0; i < 4; ++i)
+    while (tiles[i] > 8 && (M + tiles[i] - 1) / tiles[i] * tiles[i] > ws->ss_ld) tiles[i] >>= 1;
   const int NT = tiles[0];
   for (int i = 0; i < 4; ++i)
     if ((M + tiles[i] - 1) / tiles[i] * tiles[i] > ws->ss_ld) return QI_ERR_ARG;
