@@ -224,7 +224,7 @@ inline int persist_tile(int M) {
 
 // Shared-memory budget of a tensor-core projection CTA for its pipeline stages, in KB
 // (QI_TC_SMEM_KB overrides the default of 144 for tuning experiments; 144 KB measured best
-// across decode batches 1-64 and prefill, see profiles/).
+// across decode batches 1-64 and prefill).
 int tc_smem_budget_kb() {
   static int kb = -1;
   if (kb < 0) {
@@ -280,7 +280,9 @@ bool use_tc_clusters() {
 // (cached per configuration).
 int max_clusters(int epi, int NT, int stages, int C) {
   static std::map<long long, int> known;
-  const long long key = (((long long)epi * 256 + NT) * 64 + stages) * 16 + C;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const long long key = ((((long long)dev * 8 + epi) * 256 + NT) * 64 + stages) * 16 + C;
   auto it = known.find(key);
   if (it != known.end()) return it->second;
   const int n = tc_proj_max_clusters(epi, NT, stages, C);

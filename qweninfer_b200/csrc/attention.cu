@@ -57,14 +57,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 }  // namespace
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
-  static bool configured = false;
   const size_t smem_max = kMergeOffset + sizeof(ClusterMerge);
-  if (!configured) {
-    cudaError_t e =
-        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(attention_kernel), (int)smem_max);
+  if (e != cudaSuccess) return e;
   if (p.cluster && (p.max_splits < 2 || p.max_splits > kMaxClusterSplits)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.max_splits, kKvHeads, p.M);
@@ -117,7 +112,7 @@ static __device__ __align__(256) unsigned int g_attn_noalloc_scratch[kNoAllocPar
 
 namespace {
 std::mutex g_noalloc_mutex;
-void* g_noalloc_addr[64] = {};  // device address of the array, per device ordinal
+void* g_noalloc_addr[kMaxDevices] = {};  // device address of the array, per device ordinal
 }  // namespace
 
 }  // namespace qi
@@ -131,7 +126,7 @@ extern "C" int qi_attention_noalloc(const float* q, const uint16_t* k_layer, con
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return (int)e;
-  if (dev < 0 || dev >= 64) return QI_ERR_ARG;
+  if (dev < 0 || dev >= kMaxDevices) return QI_ERR_ARG;
   void* base = nullptr;
   {
     // first call on this device: resolve the array's device address (host code must not

@@ -79,7 +79,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   if (ps < 0 || ps >= p.max_len || row < 0 || (p.cache_rows > 0 && row >= p.cache_rows)) {
     // outside the cache: reported, nothing read or written; split 0 still counts the
     // (token, head) as finished for callers that wait on completions
-    if (split == 0 && tid == 0) atomicExch(p.err, QI_ERR_INDEX);
+    if (split == 0 && tid == 0 && p.err) atomicExch(p.err, QI_ERR_INDEX);
     return split == 0;
   }
   const int nkeys = ps + 1;

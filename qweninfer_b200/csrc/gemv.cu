@@ -283,11 +283,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
 template <int MT, int EPI, bool NORM>
 cudaError_t launch_one(const GemvParams& p, int ctas, int splits, size_t smem, cudaStream_t stream, bool pdl) {
   auto kern = gemv_kernel<MT, EPI, NORM>;
-  static int configured_smem = 0;
-  if ((int)smem > configured_smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  if (smem > 48 * 1024) {
+    cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), 227 * 1024);
     if (e != cudaSuccess) return e;
-    configured_smem = 227 * 1024;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas, splits, 1);

@@ -94,7 +94,14 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int M, flo
 cudaError_t launch_rope(float* q, int hq, float* k, int hk, int B, int S, const int32_t* pos, const float* cos_t,
                         const float* sin_t, cudaStream_t s);
 
+// Device ordinals the per-device caches of this library cover.
+constexpr int kMaxDevices = 64;
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// cudaFuncAttributeMaxDynamicSharedMemorySize >= bytes for `kernel` on the current device
+// (set once per device and kernel; thread-safe).
+cudaError_t set_max_dynamic_smem(const void* kernel, int bytes);
 
 }  // namespace qi

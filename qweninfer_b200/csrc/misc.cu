@@ -1,4 +1,9 @@
-// Small kernels: embedding gather into the fp32 residual stream and KV row compaction.
+// Small kernels: embedding gather into the fp32 residual stream and KV row compaction;
+// per-device launch helpers.
+#include <atomic>
+#include <map>
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 #include "tc_proj.h"
@@ -107,15 +112,31 @@ cudaError_t launch_move_rows(uint16_t* k, uint16_t* v, int layers, int cache_row
 }
 
 int sm_count() {
-  static int cached_dev = -1, cached = 148;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (dev != cached_dev) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0) cached = n;
-    cached_dev = dev;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  static std::atomic<int> cached[kMaxDevices];  // 0: not yet queried
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev].store(n, std::memory_order_relaxed);
   }
-  return cached;
+  return n;
+}
+
+// Kernel attributes are per device: a process that drives several GPUs sets them once on
+// each (the set of (device, kernel) pairs already configured is kept under a mutex).
+cudaError_t set_max_dynamic_smem(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find({dev, kernel});
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[{dev, kernel}] = bytes;
+  return e;
 }
 
 }  // namespace qi

@@ -245,7 +245,7 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
           p.q[(long long)t * kHidden + head * kHeadDim + d] = x[i];
         } else if (kv_slot_ok(p, tpos[i], trow[i])) {
           kvbase[(((long long)trow[i] * kKvHeads + kvh) * p.max_len + tpos[i]) * kHeadDim + d] = f32_to_bf16_rn(x[i]);
-        } else if (d == 0) {
+        } else if (d == 0 && p.err) {
           atomicExch(p.err, QI_ERR_INDEX);
         }
       }

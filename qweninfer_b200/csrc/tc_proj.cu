@@ -245,12 +245,8 @@ cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, boo
     case kTcLogits: kern = tc_proj_kernel<kTcLogits>; break;
     default: return cudaErrorInvalidValue;
   }
-  static bool configured[5] = {false, false, false, false, false};
-  if (!configured[p.epi]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
-    configured[p.epi] = true;
-  }
+  cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(kern), 227 * 1024);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas, 1, 1);
   cfg.blockDim = dim3(kProjThreads, 1, 1);
@@ -280,7 +276,7 @@ int tc_proj_max_clusters(int epi, int NT, int stages, int cluster) {
                            : epi == kTcSwiglu   ? tc_proj_kernel<kTcSwiglu>
                            : epi == kTcLogits   ? tc_proj_kernel<kTcLogits>
                                                 : tc_proj_kernel<kTcPlain>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) return 0;
+  if (set_max_dynamic_smem(reinterpret_cast<const void*>(kern), 227 * 1024) != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster, 1, 1);
   cfg.blockDim = dim3(kProjThreads, 1, 1);

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this directory by running the REFERENCE package.
 
-Run once, on a machine that has the reference checked out (read-only) at
-$QI_REFERENCE (default /root/reference):
+Run once, on a machine that has the reference checked out (read-only); point
+$QI_REFERENCE at its project root:
 
-    python tests/golden/make_golden.py
+    QI_REFERENCE=<path to the QwenInfer checkout> python tests/golden/make_golden.py
 
 The fixtures pin the numpy oracle (`oracle/`) to the reference's own behaviour:
 
@@ -39,7 +39,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("QI_REFERENCE", "/root/reference"))
+if not os.environ.get("QI_REFERENCE"):
+    sys.exit("set QI_REFERENCE to the QwenInfer project root (the reference checkout)")
+REF = Path(os.environ["QI_REFERENCE"])
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REF))
 

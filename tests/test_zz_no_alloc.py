@@ -56,14 +56,16 @@ def _with_scratch(t, M, max_len):
     return out.cpu().numpy()
 
 
-def _without_scratch(t, M, max_len):
+def _without_scratch(t, M, max_len, with_err: bool = True, expect_err: int = 0):
     out = torch.full((M, 896), float("nan"), device="cuda")
-    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda") if with_err else None
     _lib.check(_lib.lib().qi_attention_noalloc(
         t["q"].data_ptr(), t["k"].data_ptr(), t["v"].data_ptr(), t["pos"].data_ptr(), t["rows"].data_ptr(),
-        M, max_len, out.data_ptr(), err.data_ptr(), _lib.stream_ptr()), "qi_attention_noalloc")
+        M, max_len, out.data_ptr(), None if err is None else err.data_ptr(), _lib.stream_ptr()),
+        "qi_attention_noalloc")
     torch.cuda.synchronize()
-    assert int(err.item()) == 0
+    if err is not None:
+        assert int(err.item()) == expect_err
     return out.cpu().numpy()
 
 
@@ -75,6 +77,30 @@ def test_attention_without_allocation_matches_scratch_variant():
         ref = _with_scratch(t, M, max_len)
         got = _without_scratch(t, M, max_len)
         assert np.abs(got - ref).max() <= ATOL, (M, max_len)
+
+
+def test_attention_without_allocation_accepts_null_err():
+    """`err` may be NULL (include/qi.h): valid inputs give the same output."""
+    _lib.ensure_device(torch.device("cuda", torch.cuda.current_device()))
+    M, max_len = 6, 300
+    t = _case(M, max_len, 3)
+    ref = _with_scratch(t, M, max_len)
+    got = _without_scratch(t, M, max_len, with_err=False)
+    assert np.abs(got - ref).max() <= ATOL
+
+
+def test_attention_without_allocation_reports_out_of_cache_position():
+    """A position outside the cache is reported as QI_ERR_INDEX in `err`; nothing is read
+    or written for that token and every other token's output is unchanged."""
+    _lib.ensure_device(torch.device("cuda", torch.cuda.current_device()))
+    M, max_len, bad = 5, 400, 2
+    t = _case(M, max_len, 4)
+    ref = _with_scratch(t, M, max_len)
+    t["pos"][bad] = max_len  # one past the last slot of its row
+    got = _without_scratch(t, M, max_len, expect_err=_lib.QI_ERR_INDEX)
+    keep = [i for i in range(M) if i != bad]
+    assert np.abs(got[keep] - ref[keep]).max() <= ATOL
+    assert np.isnan(got[bad]).all()  # the bad token's output is left as it was
 
 
 def test_attention_without_allocation_rejects_oversized_calls():
