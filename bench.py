@@ -4,34 +4,37 @@ Workload (synthetic, seeded; no dataset): Qwen2-0.5B architecture (24 layers, hi
 896, 14/2 heads, intermediate 4864, vocab 151936) with seeded random bf16 weights; 96
 requests arriving at t=0, prompts uniform in [32, 256] tokens, output lengths lognormal
 (median 75, sigma 0.8) clipped to [1, 256] and generated in full (no EOS); packed KV
-cache with max_len 512; 32 slots. One bench step = one complete run of the trace
-through `Engine.run` (the prefills of each step's admissions, batched into forwards of
-up to 512 tokens, + every batched decode step + row moves).
+cache with max_len 512; 32 slots. One bench step = one complete run of the trace through
+`Engine.step`; the timed unit is the WINDOW of engine steps 50..109 of that run (60
+scheduler iterations, decode-dominated, with the admissions that fall inside it), the
+same window the reference arm times, so both arms report the same quantity.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qweninfer_b200|reference]
 
 Printed JSON (rank 0, one line):
-  value  output tokens / device time of the trace's forwards (prefill + decode graph
-         replays, CUDA events on the launching stream); host scheduling excluded.
-  e2e    output tokens / time of Engine.run through the public API, CUDA events around
-         the whole run: host bookkeeping, per-step H2D of (ids, positions, rows) from
-         pinned memory and D2H of the argmax words included.
-  roofline  the gate/up+SwiGLU tensor-core projection (tc_proj_kernel<swiglu>, the
-         largest per-layer weight stream) at the trace's mean decode batch, timed alone
-         over the 24 layers' distinct weights (418 MB > L2), achieved HBM GB/s vs the
-         measured copy peak; traffic = DRAM bytes per launch from an ncu capture
-         (profiles/tc_proj_swiglu_decode.md).
+  value   output tokens produced in the window / device time of the window's forwards
+          (CUDA events on the launching stream; max over ranks, tokens summed).
+  e2e     the same tokens / time of the window's Engine.step calls through the public
+          API (CUDA events around them): host bookkeeping, per-step H2D of (ids,
+          positions, rows) from pinned memory and D2H of the argmax words included.
+  roofline  the decode-step kernel (step_kernel: the whole forward of a decode step in
+          one launch) over the window's decode steps: algorithmic bytes per launch
+          (weights + KV read + KV write + embedding rows) / launch time vs the measured
+          HBM copy peak.
+  full_trace, batch1, prefill, serve64_padded  the other BASELINE configurations on the
+          same model (N = 1 only).
   cpu_baseline  the numpy oracle (the reference's algorithm restated) on the host cores
-         over a bounded sample of the same workload.
+          over a bounded sample of the same window.
 
 Under torchrun (N > 1) every rank runs its own replica of the trace on its own GPU
-(weak scaling, no collective on the data path); value = all ranks' tokens / max over
-ranks of the device time.
+(weak scaling, no collective on the data path).
 """
 
 from __future__ import annotations
 
 import argparse
+import copy
+from collections import deque
 import json
 import os
 import statistics
@@ -49,13 +52,13 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 MAX_LEN = 512
+WINDOW = (50, 110)                  # engine steps timed in both arms
 WEIGHT_BYTES = 988_065_536          # bf16 layer weights + norms + biases + tied head
 KV_BYTES_PER_TOKEN = 12_288         # 2 (K,V) * 24 layers * 2 heads * 64 * 2 B
-# DRAM bytes (read + write) per launch of tc_proj_kernel<swiglu> by token tile, from one
-# ncu capture of the same launch (profiles/tc_proj_swiglu_decode.md: token tile 32, the
-# batch-22 case; 16 from an earlier capture of the same kernel); None until captured.
-TRAFFIC: dict[int, int | None] = {16: 17_615_616, 32: 17_612_288}
 EMBED_ROW_BYTES = 1_792
+METRIC = "decode tok/s on 96-req continuous-batch workload"
+LAYER_PARAMS = 357_897_216          # weights of the 24 blocks
+HEAD_PARAMS = 136_134_656           # tied head (vocab x hidden)
 
 
 def parse():
@@ -65,12 +68,14 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="qweninfer_b200", choices=["qweninfer_b200", "reference"])
     ap.add_argument("--slots", type=int, default=32)
+    ap.add_argument("--no-extras", action="store_true", help="skip the other configurations (N = 1 extras)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-seconds", type=float, default=15.0)
-    ap.add_argument("--only", choices=["roofline", "decode"], default=None,
-                    help="roofline: only the timed gate/up projection loop; decode: only graph-replayed "
-                         "decode steps at --batch (the profiling cases)")
-    ap.add_argument("--batch", type=int, default=22, help="decode batch of --only roofline")
+    ap.add_argument("--cpu-window-steps", type=int, default=10,
+                    help="engine steps of the window the in-process cpu_baseline times")
+    ap.add_argument("--only", choices=["decode", "batch1", "prefill", "serve64"], default=None,
+                    help="one measurement alone (profiling cases): graph-replayed decode steps at --batch, "
+                         "config-1 batch-1 decode, config-2 prefill, config-3 64 padded slots")
+    ap.add_argument("--batch", type=int, default=22, help="decode batch of --only decode")
     return ap.parse_args()
 
 
@@ -78,8 +83,14 @@ def peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def step_bytes(pos: list[int]) -> int:
+    """Algorithmic HBM bytes of one decode step over rows at positions `pos`."""
+    B = len(pos)
+    return WEIGHT_BYTES + sum(p + 1 for p in pos) * KV_BYTES_PER_TOKEN + B * KV_BYTES_PER_TOKEN + B * EMBED_ROW_BYTES
 
 
 # ----------------------------------------------------------------- clocks
@@ -138,119 +149,145 @@ def load_model(device: torch.device):
 
 
 class TimedRunner:
-    """Wraps an engine's runner: CUDA-event device time of every forward, per-decode-step
-    algorithmic bytes, kernel launch count."""
+    """Wraps an engine's runner: CUDA-event device time of every forward (prefill and
+    decode separately), per-decode-step algorithmic bytes; `active` gates the tally."""
 
     def __init__(self, runner) -> None:
         self.r = runner
-        self.device_ms = 0.0
-        self.decode_ms = 0.0
-        self.decode_bytes = 0
-        self.decode_rows = []
+        self.active = False
+        self.reset()
         self.ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         self._prefill, self._prefill_many, self._decode = runner.prefill, runner.prefill_many, runner.decode
         runner.prefill, runner.prefill_many, runner.decode = self.prefill, self.prefill_many, self.decode
 
-    def prefill(self, row, prompt):
+    def reset(self) -> None:
+        self.prefill_ms = self.decode_ms = 0.0
+        self.decode_bytes = 0
+        self.decode_rows: list[int] = []
+        self.prefill_tokens = 0
+
+    def _timed(self, fn, *a):
         self.ev[0].record()
-        tok = self._prefill(row, prompt)
+        out = fn(*a)
         self.ev[1].record()
         self.ev[1].synchronize()
-        self.device_ms += self.ev[0].elapsed_time(self.ev[1])
+        return out, self.ev[0].elapsed_time(self.ev[1])
+
+    def prefill(self, row, prompt):
+        tok, ms = self._timed(self._prefill, row, prompt)
+        if self.active:
+            self.prefill_ms += ms
+            self.prefill_tokens += len(prompt)
         return tok
 
     def prefill_many(self, rows, prompts):
-        self.ev[0].record()
-        toks = self._prefill_many(rows, prompts)
-        self.ev[1].record()
-        self.ev[1].synchronize()
-        self.device_ms += self.ev[0].elapsed_time(self.ev[1])
+        toks, ms = self._timed(self._prefill_many, rows, prompts)
+        if self.active:
+            self.prefill_ms += ms
+            self.prefill_tokens += sum(len(p) for p in prompts)
         return toks
 
     def decode(self, toks, pos, row_start=0):
-        self.ev[0].record()
-        out = self._decode(toks, pos, row_start)
-        self.ev[1].record()
-        self.ev[1].synchronize()
-        ms = self.ev[0].elapsed_time(self.ev[1])
-        self.device_ms += ms
-        self.decode_ms += ms
-        B = len(toks)
-        self.decode_bytes += (WEIGHT_BYTES + sum(p + 1 for p in pos) * KV_BYTES_PER_TOKEN
-                              + B * KV_BYTES_PER_TOKEN + B * EMBED_ROW_BYTES)
-        self.decode_rows.append(B)
+        out, ms = self._timed(self._decode, toks, pos, row_start)
+        if self.active:
+            self.decode_ms += ms
+            self.decode_bytes += step_bytes(list(pos))
+            self.decode_rows.append(len(toks))
         return out
+
+
+def run_trace(eng, timed: TimedRunner, workload, window=WINDOW) -> dict:
+    """One full run of the trace through Engine.step; device and end-to-end time of the
+    window of engine steps [window[0], window[1]) and of the whole trace."""
+    from qweninfer_b200.engine.engine import Request
+    reqs = [Request(r.rid, r.prompt, r.max_new_tokens) for r in workload]
+    for r in reqs:
+        eng.submit(r)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    launches0 = eng.runner.launches
+    h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
+    out: dict = {}
+    step = 0
+    torch.cuda.synchronize()
+    ev[0].record()
+    full_dev = 0.0
+    while eng.waiting or eng.active:
+        if step == window[0]:
+            full_dev += timed.prefill_ms + timed.decode_ms
+            timed.reset()
+            toks0 = sum(len(r.output) for r in reqs)
+            l0, hb0, db0 = eng.runner.launches, eng.runner.h2d_bytes, eng.runner.d2h_bytes
+            ev[2].record()
+        eng.step()
+        step += 1
+        if step == window[1]:
+            ev[3].record()
+            ev[3].synchronize()
+            out["window"] = {"tokens": sum(len(r.output) for r in reqs) - toks0,
+                             "dev_ms": timed.prefill_ms + timed.decode_ms, "e2e_ms": ev[2].elapsed_time(ev[3]),
+                             "decode_ms": timed.decode_ms, "decode_bytes": timed.decode_bytes,
+                             "decode_steps": len(timed.decode_rows), "prefill_ms": timed.prefill_ms,
+                             "prefill_tokens": timed.prefill_tokens,
+                             "mean_batch": float(np.mean(timed.decode_rows)) if timed.decode_rows else 0.0,
+                             "launches": eng.runner.launches - l0, "h2d": eng.runner.h2d_bytes - hb0,
+                             "d2h": eng.runner.d2h_bytes - db0}
+            full_dev += timed.prefill_ms + timed.decode_ms
+            timed.reset()
+    ev[1].record()
+    ev[1].synchronize()
+    full_dev += timed.prefill_ms + timed.decode_ms
+    done = sorted(reqs, key=lambda r: r.rid)
+    toks = sum(len(r.output) for r in done)
+    out["full"] = {"tokens": toks, "dev_ms": full_dev, "e2e_ms": ev[0].elapsed_time(ev[1]), "steps": step,
+                   "ttft_mean_s": statistics.mean(r.first_token - r.arrival for r in done),
+                   "latency_mean_s": statistics.mean(r.finished - r.arrival for r in done),
+                   "launches": eng.runner.launches - launches0,
+                   "h2d": eng.runner.h2d_bytes - h2d0, "d2h": eng.runner.d2h_bytes - d2h0}
+    return out
 
 
 def our_arm(args, rank: int, world: int, device: torch.device) -> dict | None:
     from qweninfer_b200 import synthetic
-    from qweninfer_b200.engine.engine import Engine, Request
+    from qweninfer_b200.engine.engine import Engine
 
     model = load_model(device)
     workload = synthetic.serving96()
     eng = Engine(model, max_slots=args.slots, max_len=MAX_LEN)
     timed = TimedRunner(eng.runner)
-    moves = [0]
-    orig_move = eng.cache.move_row
-
-    def move_row(src, dst, length):
-        moves[0] += 1
-        orig_move(src, dst, length)
-
-    eng.cache.move_row = move_row
-
-    def one_trace():
-        reqs = [Request(r.rid, r.prompt, r.max_new_tokens) for r in workload]
-        done = eng.run(reqs)
-        return done
-
+    timed.active = True
     for _ in range(args.warmup):
-        one_trace()
+        run_trace(eng, timed, workload)
     eng.runner.check()
 
-    # timed region
-    tokens = 0
-    timed.device_ms = timed.decode_ms = 0.0
-    timed.decode_bytes = 0
-    timed.decode_rows = []
-    launches0, h2d0, d2h0, moves0 = eng.runner.launches, eng.runner.h2d_bytes, eng.runner.d2h_bytes, moves[0]
-    ttft, lat = [], []
     clocks = ClockSampler(device.index or 0)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     clocks.start()
-    start.record()
-    for _ in range(args.steps):
-        done = one_trace()
-        tokens += sum(len(r.output) for r in done)
-        ttft += [r.first_token - r.arrival for r in done]
-        lat += [r.finished - r.arrival for r in done]
-    stop.record()
+    runs = [run_trace(eng, timed, workload) for _ in range(args.steps)]
     torch.cuda.synchronize()
     clock_info = clocks.stop()
-    e2e_ms = start.elapsed_time(stop)
-    dev_ms = timed.device_ms
-    if world > 1:
-        t = torch.tensor([dev_ms, e2e_ms, float(tokens)], device=device, dtype=torch.float64)
-        mx = t.clone()
-        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
-        sm = t.clone()
-        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
-        dev_ms, e2e_ms, tokens_all = float(mx[0]), float(mx[1]), float(sm[2])
-        torch.distributed.barrier()
-    else:
-        tokens_all = float(tokens)
     eng.runner.check()
+    W = {k: sum(r["window"][k] for r in runs) for k in runs[0]["window"]}
+    F = {k: sum(r["full"][k] for r in runs) for k in ("tokens", "dev_ms", "e2e_ms", "launches", "h2d", "d2h")}
+    dev_ms, e2e_ms, tokens = W["dev_ms"], W["e2e_ms"], float(W["tokens"])
+    if world > 1:
+        t = torch.tensor([dev_ms, e2e_ms, tokens], device=device, dtype=torch.float64)
+        mx, sm = t.clone(), t.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
+        dev_ms, e2e_ms, tokens = float(mx[0]), float(mx[1]), float(sm[2])
+        torch.distributed.barrier()
     if rank != 0:
         return None
-
     K = args.steps
-    launches = (eng.runner.launches - launches0) + (moves[0] - moves0)
+    pk = peaks()
+    launch_s = W["decode_ms"] / 1e3 / max(1, W["decode_steps"])
+    algo = W["decode_bytes"] / max(1, W["decode_steps"])
+    gbs = algo / launch_s / 1e9
     res = {
-        "metric": "decode tok/s on 96-req continuous-batch workload",
-        "value": tokens_all / (dev_ms / 1e3),
+        "metric": METRIC,
+        "value": tokens / (dev_ms / 1e3),
         "unit": "tok/s",
         "n_gpus": world,
         "steps": K,
@@ -261,87 +298,37 @@ def our_arm(args, rank: int, world: int, device: torch.device) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded random weights of the Qwen2-0.5B architecture; seeded synthetic requests)",
-        "config": {"workload": f"serve96: 96 requests, prompts U[32,256], outputs lognormal(75,0.8)<=256, "
-                               f"{args.slots} slots, max_len {MAX_LEN}, one replica per GPU",
-                   "model": "Qwen2-0.5B architecture, random bf16 weights",
-                   "slots": args.slots, "max_len": MAX_LEN, "parallelism": f"replicas x{world}",
+        "config": {"workload": f"serve96 window: engine steps {WINDOW[0]}-{WINDOW[1] - 1} of the 96-request trace "
+                               f"(prompts U[32,256], outputs lognormal(75,0.8)<=256, seed 4), {args.slots} slots, "
+                               f"max_len {MAX_LEN}, one replica per GPU",
+                   "model": "Qwen2-0.5B architecture, random bf16 weights", "slots": args.slots,
+                   "max_len": MAX_LEN, "window": list(WINDOW), "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2: every decode step streams 988 MB of weights"},
-        "e2e": {"value": tokens_all / (e2e_ms / 1e3), "unit": "tok/s",
-                "h2d_bytes_per_step": (eng.runner.h2d_bytes - h2d0) // K,
-                "d2h_bytes_per_step": (eng.runner.d2h_bytes - d2h0) // K,
-                "ms_per_step": e2e_ms / K},
-        "gpu_launches": launches,
-        "serving": {"output_tokens_per_trace": tokens // K, "ttft_mean_s": statistics.mean(ttft),
-                    "latency_mean_s": statistics.mean(lat),
-                    "decode_steps_per_trace": len(timed.decode_rows) // K,
-                    "mean_decode_batch": float(np.mean(timed.decode_rows)),
-                    "decode_ms_per_step": timed.decode_ms / max(1, len(timed.decode_rows)),
-                    "prefill_ms_total_per_trace": (timed.device_ms - timed.decode_ms) / K},
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": W["h2d"] // K,
+                "d2h_bytes_per_step": W["d2h"] // K, "ms_per_step": e2e_ms / K},
+        "gpu_launches": W["launches"],
+        "window": {"output_tokens_per_step": W["tokens"] // K, "decode_steps_per_step": W["decode_steps"] // K,
+                   "mean_decode_batch": W["mean_batch"] / K, "decode_ms_per_decode_step": launch_s * 1e3,
+                   "prefill_ms_per_step": W["prefill_ms"] / K, "prefill_tokens_per_step": W["prefill_tokens"] // K},
+        "roofline": {"kernel": "step_kernel: the whole decode-step forward in one cooperative launch (embedding, "
+                               "24 layers, head + argmax), over the window's decode steps", "bound": "hbm",
+                     "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"],
+                     "peak_source": pk["source"], "traffic": None,
+                     "algorithmic_bytes_per_launch": algo, "us_per_launch": launch_s * 1e6,
+                     "bytes": "988,065,536 weights + sum(len+1)*12,288 KV read + B*12,288 KV write + B*1,792 "
+                              "embed, per decode step"},
+        "full_trace": {"value": F["tokens"] / (F["dev_ms"] / 1e3), "e2e": F["tokens"] / (F["e2e_ms"] / 1e3),
+                       "unit": "tok/s", "output_tokens": F["tokens"] // K, "engine_steps": runs[0]["full"]["steps"],
+                       "ttft_mean_s": statistics.mean(r["full"]["ttft_mean_s"] for r in runs),
+                       "latency_mean_s": statistics.mean(r["full"]["latency_mean_s"] for r in runs),
+                       "gpu_launches_per_trace": F["launches"] // K},
         "clocks": clock_info,
     }
-    pk = peaks()
-    step_gbs = timed.decode_bytes / (timed.decode_ms / 1e3) / 1e9
-    res["decode_step_roofline"] = {"bound": "hbm", "achieved": step_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                                   "frac": step_gbs / pk["hbm_gbs"], "peak_source": pk["source"],
-                                   "bytes": "988,065,536 weights + sum(len+1)*12,288 KV read + B*12,288 KV "
-                                            "write + B*1,792 embed, per decode step"}
-    res["roofline"] = kernel_roofline(model, int(round(np.mean(timed.decode_rows))), pk)
-    res["batch1"] = batch1_latency(model)
+    if world == 1 and not args.no_extras:
+        res["batch1"] = batch1_latency(model, pk)
+        res["prefill"] = prefill_ttft(model, pk)
+        res["serve64_padded"] = serve64(model)
     return res
-
-
-def kernel_roofline(model, M: int, pk: dict) -> dict:
-    """The forward's gate/up + SwiGLU projection (tc_proj_kernel<swiglu>, the launch
-    qi_forward issues for it, through qi_tc_gate_up_swiglu) at decode batch M, cycling
-    through the 24 layers' distinct weights (418 MB > L2), CUDA events on its stream."""
-    import ctypes as C
-    from qweninfer_b200 import _lib
-    from qweninfer_b200.models.qwen2 import gate_up_tile
-    dev = model.device
-    NT = gate_up_tile(M)
-    Mp = -(-M // NT) * NT
-    L = _lib.lib()
-    s = _lib.stream_ptr(dev)
-    x = torch.randn(M, 896, device=dev)
-    nw = model.layers[0].post_attention_layernorm.weight.float().contiguous()
-    act = torch.zeros(Mp * 896 * 2, dtype=torch.int16, device=dev)
-    ss = torch.zeros(7 * Mp, device=dev)
-    _lib.check(L.qi_act_tiles(x.data_ptr(), nw.data_ptr(), M, 896, NT, act.data_ptr(), ss.data_ptr(), Mp, s),
-               "act_tiles")
-    out = torch.zeros(Mp * 4864 * 2, dtype=torch.int16, device=dev)
-    scratch = torch.empty(148 * 2 * 128 * NT, device=dev)
-    counters = torch.zeros(1024, dtype=torch.int32, device=dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    ws = [blk.mlp.w_gate_up_tiled.data_ptr() for blk in model.layers]
-
-    def launch_all():
-        for w in ws:
-            _lib.check(L.qi_tc_gate_up_swiglu(w, act.data_ptr(), M, NT, ss.data_ptr(), Mp, C.c_float(1e-6),
-                                              out.data_ptr(), scratch.data_ptr(), scratch.numel(),
-                                              counters.data_ptr(), counters.numel(), 0, err.data_ptr(), s),
-                       "tc_gate_up_swiglu")
-
-    for _ in range(3):
-        launch_all()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 20
-    a.record()
-    for _ in range(reps):
-        launch_all()
-    b.record()
-    b.synchronize()
-    if int(err.item()) != 0:
-        raise RuntimeError("gate/up kernel reported an error")
-    per_launch_s = a.elapsed_time(b) / 1e3 / (reps * len(ws))
-    # algorithmic bytes: weights once, activation tiles in (hi/lo bf16), the 7 partial sums
-    # of squares, SwiGLU activation tiles out (hi/lo bf16), for the M live tokens
-    algo = 9728 * 896 * 2 + M * 896 * 4 + 7 * M * 4 + M * 4864 * 4
-    gbs = algo / per_launch_s / 1e9
-    return {"kernel": "tc_proj_kernel<swiglu>: RMSNorm-folded gate/up projection + SwiGLU (tcgen05, bulk-copy "
-                      "ring, the forward's stream-K partition), the forward's largest weight stream", "bound": "hbm",
-            "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"],
-            "peak_source": pk["source"], "traffic": TRAFFIC.get(NT), "batch": M, "token_tile": NT,
-            "us_per_launch": per_launch_s * 1e6, "algorithmic_bytes_per_launch": algo}
 
 
 def decode_steps(model, B: int, steps: int, warmup: int) -> dict:
@@ -360,44 +347,108 @@ def decode_steps(model, B: int, steps: int, warmup: int) -> dict:
     b.record()
     b.synchronize()
     r.check()
-    return {"batch": B, "steps": steps, "ms_per_step": a.elapsed_time(b) / steps}
+    ms = a.elapsed_time(b) / steps
+    byts = step_bytes([200 + warmup + steps // 2] * B)
+    return {"batch": B, "steps": steps, "ms_per_step": ms, "hbm_gbs": byts / (ms / 1e3) / 1e9}
 
 
-def batch1_latency(model) -> dict:
-    """Batch-1 decode ms/token at contexts 16/256/1024 (128 tokens each, CUDA events)."""
+def batch1_latency(model, pk: dict) -> dict:
+    """Config 1: batch-1 decode at contexts 16/256/1024 (seed-2 prompts, prefill then 128
+    greedy tokens), ms/token (CUDA events over the decode steps) and HBM fraction."""
     from qweninfer_b200 import synthetic
     from qweninfer_b200.engine.kv_cache import KVCache
     from qweninfer_b200.engine.runner import DecodeRunner
     out = {}
-    prompts = synthetic.decode_latency_prompts()
-    for C_, prompt in prompts.items():
+    for C_, prompt in synthetic.decode_latency_prompts().items():
         cache = KVCache(model.cfg, 1, C_ + 130, dtype=torch.bfloat16, device=model.device)
         r = DecodeRunner(model, cache, max_batch=1)
         tok = r.prefill(0, prompt)
         for i in range(3):
             tok = int(r.decode([tok], [C_ + i])[0])
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
         n = 125
+        a.record()
         for i in range(n):
             tok = int(r.decode([tok], [C_ + 3 + i])[0])
         b.record()
         b.synchronize()
+        r.check()
         ms = a.elapsed_time(b) / n
-        byts = WEIGHT_BYTES + (C_ + 64) * KV_BYTES_PER_TOKEN
-        out[str(C_)] = {"ms_per_token": ms, "hbm_gbs": byts / (ms / 1e3) / 1e9}
+        byts = step_bytes([C_ + 3 + n // 2])
+        gbs = byts / (ms / 1e3) / 1e9
+        out[str(C_)] = {"ms_per_token": ms, "hbm_gbs": gbs, "frac": gbs / pk["hbm_gbs"]}
         del r, cache
     return out
 
 
+def prefill_ttft(model, pk: dict) -> dict:
+    """Config 2: batch-1 causal prefill of seed-3 prompts of 64/256/512/1024 tokens writing
+    the cache and emitting the first greedy token; TTFT (CUDA events, median of 5 after a
+    warm-up) and the achieved dense rate: 2 * (block params * P + head params) plus the
+    causal attention products 2 * 2 * layers * heads * head_dim * P(P+1)/2."""
+    from qweninfer_b200 import synthetic
+    from qweninfer_b200.engine.kv_cache import KVCache
+    from qweninfer_b200.engine.runner import DecodeRunner
+    out = {}
+    for P, prompt in synthetic.prefill_prompts().items():
+        cache = KVCache(model.cfg, 1, P, dtype=torch.bfloat16, device=model.device)
+        r = DecodeRunner(model, cache, max_batch=1)
+        r.prefill(0, prompt)
+        ts = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            r.prefill(0, prompt)
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        r.check()
+        ms = statistics.median(ts)
+        flops = 2 * (LAYER_PARAMS * P + HEAD_PARAMS) + 4 * 24 * 14 * 64 * P * (P + 1) / 2
+        tflops = flops / (ms / 1e3) / 1e12
+        out[str(P)] = {"ttft_ms": ms, "tflops": tflops, "frac_of_bf16_peak": tflops / pk["bf16_tflops"]
+                       if pk.get("bf16_tflops") else None}
+        del r, cache
+    return out
+
+
+def serve64(model) -> dict:
+    """Config 3, second arm: 64 slots with autotuned padding (autotune_padding on this
+    GPU, then the full 96-request trace)."""
+    from qweninfer_b200 import synthetic
+    from qweninfer_b200.engine.engine import Engine, autotune_padding
+    pad_to, ms = autotune_padding(model, 64)
+    eng = Engine(model, max_slots=64, max_len=MAX_LEN, pad_to=pad_to)
+    timed = TimedRunner(eng.runner)
+    timed.active = True
+    run_trace(eng, timed, synthetic.serving96())
+    r = run_trace(eng, timed, synthetic.serving96())["full"]
+    eng.runner.check()
+    return {"value": r["tokens"] / (r["dev_ms"] / 1e3), "e2e": r["tokens"] / (r["e2e_ms"] / 1e3), "unit": "tok/s",
+            "ttft_mean_s": r["ttft_mean_s"], "latency_mean_s": r["latency_mean_s"],
+            "pad_sizes": sorted(set(pad_to[1:])), "autotune_ms": {str(k): v for k, v in ms.items()}}
+
+
 # ------------------------------------------------------------- CPU arms
 
-def cpu_sample(seconds: float) -> dict:
-    """The numpy oracle (the reference's fp32 algorithm) on this host's cores: the serving
-    trace (32 slots) run from its start until `seconds` of work, as tok/s."""
+def cpu_threads() -> int:
+    """Use every host thread for numpy (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+    from threadpoolctl import threadpool_limits
+    n = os.cpu_count() or 1
+    threadpool_limits(limits=n)
+    return n
+
+
+def oracle_window(n_steps: int, samples: int, warmup: int) -> dict:
+    """The numpy oracle (the reference's fp32 algorithm) on the host cores: the serving
+    trace (32 slots) is brought to engine step WINDOW[0] by the scheduler's bookkeeping
+    alone (no arithmetic; the KV prefix rows stay zero, which changes no operation count),
+    then `n_steps` engine steps are timed with full arithmetic from that state, `samples`
+    times (after `warmup` untimed single steps). Returns tokens per second."""
     from oracle import OracleModel, OracleRequest, bf16_round
-    from oracle.engine_ref import OracleEngine
+    from oracle.engine_ref import OracleEngine, StubModel
     from qweninfer_b200 import synthetic
+    threads = cpu_threads()
     cfg = synthetic.full_config()
     state = {k: bf16_round(v.numpy()) for k, v in synthetic.synthetic_state(cfg, 0).items()}
     oracle = OracleModel(state, vars(cfg))
@@ -406,35 +457,59 @@ def cpu_sample(seconds: float) -> dict:
     reqs = [OracleRequest(r.rid, r.prompt, r.max_new_tokens) for r in synthetic.serving96()]
     for r in reqs:
         eng.submit(r)
-    t0 = time.perf_counter()
-    steps = 0
-    while (eng.waiting or eng.active) and time.perf_counter() - t0 < seconds:
+    eng.model = StubModel(cfg.vocab_size)
+    for _ in range(WINDOW[0]):
         eng.step()
-        steps += 1
-    dt = time.perf_counter() - t0
-    toks = sum(len(r.output) for r in reqs)
-    return {"value": toks / dt, "unit": "tok/s", "cores": os.cpu_count() or 1,
-            "kind": "port", "sample": f"first {steps} engine steps of the 96-request trace (32 slots) "
-                                       f"through the numpy oracle (fp32, all host threads), {dt:.1f} s, "
-                                       f"{toks} output tokens"}
+    eng.model = oracle
+    # every sample starts from the same state: the cache and the scheduler's queues
+    snap_k, snap_v = eng.cache.k.copy(), eng.cache.v.copy()
+    snap_q = copy.deepcopy((list(eng.waiting), list(eng.active)))
+
+    def restore() -> list:
+        eng.cache.k[...] = snap_k
+        eng.cache.v[...] = snap_v
+        w, a = copy.deepcopy(snap_q)
+        eng.waiting, eng.active = deque(w), a
+        return w + a
+
+    for _ in range(warmup):
+        restore()
+        eng.step()
+    per = []
+    for _ in range(samples):
+        live = restore()
+        t0 = sum(len(r.output) for r in live)
+        s0 = time.perf_counter()
+        for _ in range(n_steps):
+            if not (eng.waiting or eng.active):
+                break
+            eng.step()
+        dt = time.perf_counter() - s0
+        per.append((sum(len(r.output) for r in live) - t0, dt))
+    toks = sum(t for t, _ in per)
+    secs = sum(d for _, d in per)
+    return {"value": toks / secs, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"engine steps {WINDOW[0]}-{WINDOW[0] + n_steps - 1} of the 96-request trace (32 slots) "
+                      f"through the numpy oracle (fp32, {threads} host threads), {samples} sample(s), "
+                      f"{toks // samples} output tokens and {secs / samples:.1f} s each; the state at step "
+                      f"{WINDOW[0]} reached by bookkeeping alone"}
 
 
 def reference_arm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    per = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_sample(args.cpu_sample_seconds / 3)
-        if i >= args.warmup:
-            per.append(r)
-    v = statistics.mean(p["value"] for p in per)
-    line = {"impl": "reference", "metric": "decode tok/s on 96-req continuous-batch workload", "value": v,
-            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": "serve96, 32 slots, max_len 512 (bounded sample)"},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": per[0]["cores"], "kind": "port",
-                             "sample": per[0]["sample"]},
-            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    r = oracle_window(WINDOW[1] - WINDOW[0], max(1, args.steps), args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"serve96 window: engine steps {WINDOW[0]}-{WINDOW[1] - 1} of the 96-request "
+                                   f"trace (prompts U[32,256], outputs lognormal(75,0.8)<=256, seed 4), "
+                                   f"{args.slots} slots, max_len {MAX_LEN}, one replica per GPU",
+                       "model": "Qwen2-0.5B architecture, random bf16 weights", "slots": args.slots,
+                       "max_len": MAX_LEN, "window": list(WINDOW), "parallelism": f"replicas x{world}",
+                       "l2": "inputs larger than L2: every decode step streams 988 MB of weights"},
+            "cpu_baseline": r,
+            "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -448,11 +523,13 @@ def main() -> None:
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if args.only == "roofline":
-        print(json.dumps(kernel_roofline(load_model(device), args.batch, peaks())), flush=True)
-        return
-    if args.only == "decode":
-        print(json.dumps(decode_steps(load_model(device), args.batch, args.steps, args.warmup)), flush=True)
+    if args.only is not None:
+        model = load_model(device)
+        pk = peaks()
+        r = {"decode": lambda: decode_steps(model, args.batch, args.steps, args.warmup),
+             "batch1": lambda: batch1_latency(model, pk), "prefill": lambda: prefill_ttft(model, pk),
+             "serve64": lambda: serve64(model)}[args.only]()
+        print(json.dumps(r), flush=True)
         return
     if world > 1:
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
@@ -461,7 +538,7 @@ def main() -> None:
         if rank == 0 and res is not None:
             if world == 1 and not args.no_cpu_baseline:
                 try:
-                    res["cpu_baseline"] = cpu_sample(args.cpu_sample_seconds)
+                    res["cpu_baseline"] = oracle_window(args.cpu_window_steps, 1, 0)
                 except Exception as e:  # the baseline must not hide the GPU result
                     res["cpu_baseline"] = {"error": repr(e)}
             print(json.dumps(res), flush=True)

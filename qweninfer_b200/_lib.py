@@ -48,8 +48,7 @@ class QiWorkspace(C.Structure):
                 ("attn_counters", vp), ("max_tokens", i32), ("max_splits", i32),
                 ("split_keys", i32), ("err", vp), ("use_tc", i32), ("act_x", vp), ("act_attn", vp),
                 ("act_h", vp), ("ss", vp), ("ss_ld", i32), ("tc_scratch", vp), ("tc_scratch_floats", i64),
-                ("tc_counters", vp), ("tc_counters_len", i32), ("persist_done", vp), ("persist_done_len", i32),
-                ("persist_trace", vp)]
+                ("tc_counters", vp), ("tc_counters_len", i32), ("step_counters", vp), ("step_counters_len", i32)]
 
 
 # name -> (restype, argtypes), exactly the declarations of include/qi.h
@@ -70,10 +69,8 @@ SIGNATURES = {
     "qi_move_rows": (i32, [vp, vp, i32, i32, i32, C.POINTER(i32), i32, vp]),
     "qi_forward": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp,
                          i32, i32, i32, i32, vp, i32, i64, vp, vp]),
-    "qi_persistent_stage_bytes": (i64, []),
-    "qi_persistent_plan": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp, i32,
-                                 i32, i32, i32, vp, i32, i64, vp, vp, i64, C.POINTER(i32)]),
-    "qi_persistent_launch": (i32, [vp, i32, C.POINTER(QiWorkspace), i32, vp]),
+    "qi_decode_step": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp, i32, vp,
+                             i32, i64, vp, vp]),
     "qi_act_tiles": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp]),
     "qi_tc_linear": (i32, [vp, i32, i32, vp, i32, i32, vp, i32, f32, vp, i32, vp, i64, vp, i32, i32, vp, vp]),
     "qi_tc_gate_up_swiglu": (i32, [vp, vp, i32, i32, vp, i32, f32, vp, vp, i64, vp, i32, i32, vp, vp]),

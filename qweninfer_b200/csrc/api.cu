@@ -9,7 +9,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "tc_proj.h"
-#include "persistent.h"
+#include "step.h"
 
 #include <map>
 #include <vector>
@@ -212,14 +212,6 @@ void token_tiles(int M, int nt[4]) {
   const int t = token_tile(M);
   const int gu = M <= 8 ? 8 : M <= 32 ? 32 : M <= 384 ? 64 : 128;
   for (int i = 0; i < 4; ++i) nt[i] = env[i] ? env[i] : (i == 2 ? gu : t);
-}
-
-// Token tile of the persistent forward: one tile covers all M <= 128 tokens (the power of
-// two >= M, at least 8); its stage table has a single token tile per projection.
-inline int persist_tile(int M) {
-  int nt = 8;
-  while (nt < M && nt < 128) nt <<= 1;
-  return nt;
 }
 
 // Shared-memory budget of a tensor-core projection CTA for its pipeline stages, in KB
@@ -500,212 +492,71 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
   return QI_OK;
 }
 
-// Stage table of the persistent forward (forward_persistent.cu): the same projections,
-// epilogues, attention and embedding as forward_tc, each with the CTA subset and
-// completion target it uses, and the stage it waits for.
-int plan_persistent(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
-                    const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
-                    void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots,
-                    std::vector<PStage>& out) {
-  const int NT = persist_tile(M);
-  if (M > 128 || M > ws->ss_ld || !ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss || !ws->tc_scratch ||
-      !ws->tc_counters || !ws->err)
-    return QI_ERR_ARG;
-  int lg = 0;
-  while ((1 << lg) < NT) ++lg;
-  if (ws->tc_scratch_floats < (long long)sm_count() * 2 * 128 * NT) return QI_ERR_ARG;
-  TcParams base = {};
-  base.NT = NT;
-  base.lg_nt = lg;
-  base.out_nt = NT;
-  base.lg_out_nt = lg;
-  base.n_ntiles = 1;
-  base.M = M;
-  base.ss_ld = ws->ss_ld;
-  base.eps = model->eps;
-  base.err = ws->err;
-  base.scratch = ws->tc_scratch;
-  base.counters = ws->tc_counters;
-  out.clear();
-  int caps[5];
-  tc_caps(caps, NT);  // the same partition as forward_tc: results are bitwise identical
-  PStage e = {};
-  e.kind = kPEmbed;
-  e.dep = -1;
-  e.target = M;
-  e.tc = base;
-  e.em.table = model->embed;
-  e.em.vocab = model->vocab;
-  e.em.ids = ids;
-  e.em.norm_w = model->layers[0].ln1;
-  e.em.x = ws->x;
-  e.em.act = ws->act_x;
-  e.em.ss = ws->ss;
-  e.em.slots = slots;
-  e.em.n_slots = n_head;
-  out.push_back(e);
-  auto gemm = [&](const TcParams& p, int dep, int cap) {
-    PStage g = {};
-    g.kind = kPGemm;
-    g.dep = dep;
-    g.target = p.n_mtiles * p.n_ntiles;
-    g.ctas = grid_for(p.n_mtiles * p.n_ntiles, p.KB, cap);  // CTAs that take part
-    g.tc = p;
-    out.push_back(g);
-    return (int)out.size() - 1;
-  };
-  const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
-  int prev = 0;
-  for (int li = 0; li < model->num_layers; ++li) {
-    const qi_layer& L = model->layers[li];
-    uint16_t* kl = cache->k + li * layer_elems;
-    uint16_t* vl = cache->v + li * layer_elems;
-    TcParams p = base;
-    p.w = L.w_qkv;
-    p.KB = kHidden / 64;
-    p.n_mtiles = kQkvRows / 128;
-    p.act_in = ws->act_x;
-    p.ss_in = ws->ss;
-    p.epi = kTcQkvRope;
-    p.bias = L.b_qkv;
-    p.rope_cos = model->rope_cos;
-    p.rope_sin = model->rope_sin;
-    p.pos = pos;
-    p.rows = rows;
-    p.q = ws->q;
-    p.kc = kl;
-    p.vc = vl;
-    p.max_len = cache->max_len;
-    p.cache_rows = cache->cache_rows;
-    const int s_qkv = gemm(p, prev, caps[0]);
-    PStage a = {};
-    a.kind = kPAttn;
-    a.dep = s_qkv;
-    a.target = M * kKvHeads;
-    a.tc = base;
-    a.at.q = ws->q;
-    a.at.kc = kl;
-    a.at.vc = vl;
-    a.at.pos = pos;
-    a.at.rows = rows;
-    a.at.M = M;
-    a.at.max_len = cache->max_len;
-    a.at.cache_rows = cache->cache_rows;
-    a.at.split_keys = ws->split_keys;
-    a.at.max_splits = ws->max_splits;
-    a.at.out = nullptr;
-    a.at.out_act = ws->act_attn;
-    a.at.out_nt = NT;
-    a.at.part = ws->attn_part;
-    a.at.counters = ws->attn_counters;
-    a.at.err = ws->err;
-    out.push_back(a);
-    const int s_attn = (int)out.size() - 1;
-    p = base;
-    p.w = L.w_o;
-    p.KB = kHidden / 64;
-    p.n_mtiles = kHidden / 128;
-    p.act_in = ws->act_attn;
-    p.epi = kTcResidual;
-    p.x = ws->x;
-    p.next_norm_w = L.ln2;
-    p.act_out = ws->act_x;
-    p.ss_out = ws->ss;
-    const int s_o = gemm(p, s_attn, caps[1]);
-    p = base;
-    p.w = L.w_gate_up;
-    p.KB = kHidden / 64;
-    p.n_mtiles = kGateUpRows / 128;
-    p.act_in = ws->act_x;
-    p.ss_in = ws->ss;
-    p.epi = kTcSwiglu;
-    p.act_out = ws->act_h;
-    const int s_gu = gemm(p, s_o, caps[2]);
-    p = base;
-    p.w = L.w_down;
-    p.KB = kInter / 64;
-    p.n_mtiles = kHidden / 128;
-    p.act_in = ws->act_h;
-    p.epi = kTcResidual;
-    p.x = ws->x;
-    p.next_norm_w = li + 1 < model->num_layers ? model->layers[li + 1].ln1 : model->norm;
-    p.act_out = ws->act_x;
-    p.ss_out = ws->ss;
-    prev = gemm(p, s_gu, caps[3]);
-  }
-  if (n_head > 0) {
-    TcParams p = base;
-    p.w = model->embed;
-    p.KB = kHidden / 64;
-    p.n_mtiles = model->vocab / 128;
-    p.act_in = ws->act_x;
-    p.ss_in = ws->ss;
-    p.epi = kTcLogits;
-    p.logits = logits;
-    p.logits_bf16 = logits_bf16;
-    p.logits_ld = logits_ld;
-    p.argmax = slots;
-    p.head_lo = head_lo;
-    p.head_hi = head_lo + (n_head - 1) * head_stride + 1;
-    p.head_stride = head_stride;
-    gemm(p, prev, caps[4]);
-  }
-  return QI_OK;
-}
-
-int launch_persistent_table(const void* table, int n_stages, const qi_workspace* ws, int M, cudaStream_t s) {
-  if (!table || n_stages <= 0 || !ws || !ws->persist_done || (long long)n_stages * kDoneStride > ws->persist_done_len ||
-      M <= 0 || M > 128)
-    return QI_ERR_ARG;
-  PParams P = {};
-  P.stages = static_cast<const PStage*>(table);
-  P.n_stages = n_stages;
-  P.done = ws->persist_done;
-  P.M = M;
-  P.NT = persist_tile(M);
-  P.ring = persistent_ring(P.NT);
-  uint32_t cols = 32;
-  while (cols < (uint32_t)(4 * P.NT)) cols <<= 1;
-  P.tmem_cols = cols;
-  P.err = ws->err;
-  P.trace = ws->persist_trace;
-  cudaError_t e = cudaMemsetAsync(ws->persist_done, 0, sizeof(unsigned int) * kDoneStride * (size_t)n_stages, s);
-  if (e != cudaSuccess) return (int)e;
-  return rc(launch_persistent(P, sm_count(), s));
-}
-
 }  // namespace
 
 extern "C" {
 
-long long qi_persistent_stage_bytes(void) { return (long long)sizeof(PStage); }
-
-int qi_persistent_plan(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
-                       const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
-                       void* logits, int logits_bf16, long long logits_ld, unsigned long long* argmax_slots,
-                       void* host_table, long long table_bytes, int* n_stages) {
-  if (!model || !cache || !ws || !model->layers || !host_table || !n_stages || M <= 0 || n_head < 0 ||
-      (n_head > 0 && (head_lo < 0 || head_stride < 1 || (long long)head_lo + (long long)(n_head - 1) * head_stride >= M ||
-                      !argmax_slots)) ||
-      bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || (logits && logits_ld < model->vocab) ||
-      model->vocab % kTileRows != 0 || model->num_layers <= 0 || ws->split_keys % 128 != 0 ||
-      (long long)ws->split_keys * ws->max_splits < cache->max_len || ws->max_splits > kMaxAttnSplits)
+int qi_decode_step(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
+                   const int32_t* pos, const int32_t* rows, int M, void* logits, int logits_bf16, long long logits_ld,
+                   unsigned long long* argmax_slots, qi_stream_t stream) {
+  using namespace qi::step;
+  if (!model || !cache || !ws || !model->layers || M <= 0 || M > kMaxTokens || M > ws->max_tokens ||
+      model->num_layers <= 0 || model->num_layers > kMaxLayers || model->vocab % kTileRows != 0 ||
+      bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || bad_ptr(argmax_slots) || (logits && logits_ld < model->vocab) ||
+      ws->split_keys <= 0 || ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len ||
+      ws->max_splits > kMaxAttnSplits || !ws->x || !ws->q || !ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss ||
+      !ws->tc_scratch || !ws->attn_part || !ws->attn_counters || !ws->err || !ws->step_counters)
     return QI_ERR_ARG;
-  std::vector<PStage> st;
-  const int r = plan_persistent(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits,
-                                logits_bf16, logits_ld, argmax_slots, st);
-  if (r != QI_OK) return r;
-  if ((long long)(st.size() * sizeof(PStage)) > table_bytes) return QI_ERR_ARG;
-  memcpy(host_table, st.data(), st.size() * sizeof(PStage));
-  *n_stages = (int)st.size();
-  return QI_OK;
+  const int NT = M <= 8 ? 8 : M <= 16 ? 16 : 32;
+  if (cache->max_len > model->max_seq || ws->ss_ld < NT || ws->tc_scratch_floats < (long long)kGrid * NT + (long long)kDownRanges * NT * kHidden ||
+      ws->step_counters_len < kCounterStride * (1 + kPhasesPerLayer * model->num_layers))
+    return QI_ERR_ARG;
+  if (!step_supported()) return QI_ERR_DEVICE;
+  StepParams P;
+  memset(&P, 0, sizeof(P));
+  for (int l = 0; l < model->num_layers; ++l) {
+    const qi_layer& L = model->layers[l];
+    P.L[l] = StepLayer{L.w_qkv, L.w_o, L.w_gate_up, L.w_down, L.b_qkv, L.ln1, L.ln2};
+  }
+  P.n_layers = model->num_layers;
+  P.embed = model->embed;
+  P.vocab = model->vocab;
+  P.norm_w = model->norm;
+  P.eps = model->eps;
+  P.rope_cos = model->rope_cos;
+  P.rope_sin = model->rope_sin;
+  P.ids = ids;
+  P.pos = pos;
+  P.rows = rows;
+  P.M = M;
+  P.NT = NT;
+  P.kc = cache->k;
+  P.vc = cache->v;
+  P.layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
+  P.cache_rows = cache->cache_rows;
+  P.max_len = cache->max_len;
+  P.x = ws->x;
+  P.q = ws->q;
+  P.act_x = ws->act_x;
+  P.act_attn = ws->act_attn;
+  P.act_h = ws->act_h;
+  P.ss = ws->ss;
+  P.ss_o = ws->tc_scratch;
+  P.dpart = ws->tc_scratch + (long long)kGrid * NT;
+  P.apart = ws->attn_part;
+  P.acnt = ws->attn_counters;
+  P.split_keys = ws->split_keys;
+  P.max_splits = ws->max_splits;
+  P.ctr = ws->step_counters;
+  P.logits = logits;
+  P.logits_bf16 = logits_bf16;
+  P.logits_ld = logits_ld;
+  P.argmax = argmax_slots;
+  P.err = ws->err;
+  P.slots = step_ring_slots(NT);
+  P.tmem_cols = NT <= 8 ? 64 : NT <= 16 ? 128 : 256;
+  return rc(launch_step(P, as_stream(stream)));
 }
-
-int qi_persistent_launch(const void* device_table, int n_stages, const qi_workspace* ws, int M, qi_stream_t stream) {
-  return launch_persistent_table(device_table, n_stages, ws, M, as_stream(stream));
-}
-
-
 
 int qi_version(void) { return kVersion; }
 
@@ -877,7 +728,8 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
       (n_head > 0 && (head_lo < 0 || head_stride < 1 || (long long)head_lo + (long long)(n_head - 1) * head_stride >= M)) ||
       bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || (n_head > 0 && bad_ptr(argmax_slots)) ||
       (logits && logits_ld < model->vocab) || model->vocab % kTileRows != 0 || model->num_layers <= 0 ||
-      ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len || ws->max_splits > kMaxAttnSplits)
+      ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len ||
+      ws->max_splits > kMaxAttnSplits || cache->max_len > model->max_seq)
     return QI_ERR_ARG;
   if (ws->use_tc) return forward_tc(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits,
                                     logits_bf16, logits_ld, argmax_slots, as_stream(stream));

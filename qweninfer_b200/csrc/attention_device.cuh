@@ -1,13 +1,11 @@
-// One attention work unit — (key split, KV head, query token) — as a device function shared
-// by the standalone attention kernel (attention.cu) and the persistent forward
-// (forward_persistent.cu). NW warps run a unit: warp w takes keys 32*(w % 4).. of every
-// 128-key tile and, with NW = 8, half of the 7 query heads (w / 4 picks the half). With
-// one CTA per SM the per-warp chain of dependent shared-memory loads, FMAs and shuffles
-// sets the tile time, so the standalone kernel uses 8 warps; the persistent forward runs
-// units on its 4 epilogue warps (NW = 4, all heads per warp). Every head's arithmetic is
-// the same in both forms. `sync` is the whole CTA in the standalone kernel and a named
-// barrier of the four epilogue warps in the persistent one. The two K/V stage mbarriers
-// are initialised once per CTA; `uses` carries their phase counts from unit to unit.
+// One attention work unit — (key split, KV head, query token) — as a device function of
+// the standalone attention kernel (attention.cu). NW warps run a unit: warp w takes keys
+// 32*(w % 4).. of every 128-key tile and, with NW = 8, half of the 7 query heads (w / 4
+// picks the half). With one CTA per SM the per-warp chain of dependent shared-memory
+// loads, FMAs and shuffles sets the tile time, so the kernel uses 8 warps (NW = 4 runs all
+// heads per warp, with `sync` a named barrier of those 4 warps when kNamedBarrier is set;
+// otherwise the whole CTA). The two K/V stage mbarriers are initialised once per CTA;
+// `uses` carries their phase counts from unit to unit.
 #pragma once
 
 #include "common.cuh"

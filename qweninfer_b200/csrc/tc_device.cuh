@@ -1,5 +1,5 @@
-// Device-side building blocks shared by the tensor-core kernels (tc_proj.cu and the
-// persistent forward in forward_persistent.cu): tcgen05 / TMEM wrappers, UMMA
+// Device-side building blocks of the tensor-core kernels (tc_proj.cu, and the tcgen05 /
+// TMEM wrappers and descriptors the decode-step kernel in step.cu uses): UMMA
 // descriptors, the stream-K partition, activation-tile addressing and the fused
 // epilogues of every projection.
 #pragma once
@@ -11,7 +11,6 @@
 namespace qi {
 namespace tc {
 
-constexpr int kThreads = 192;        // producer, MMA issuer, 4 epilogue warps (persistent kernel)
 constexpr int kProjEpiWarps = 8;      // epilogue warps of tc_proj_kernel: two per TMEM lane quadrant
 constexpr int kProjThreads = 64 + 32 * kProjEpiWarps;
 constexpr int kEpiWarp0 = 2;
@@ -56,8 +55,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
-// named barrier of the four epilogue warps
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 // named barrier of EW epilogue warps
 template <int EW>
 __device__ __forceinline__ void epi_bar_n() {

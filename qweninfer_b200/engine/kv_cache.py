@@ -23,11 +23,14 @@ from qweninfer_b200.models.config import Qwen2Config
 class KVCache:
     def __init__(self, cfg: Qwen2Config, max_batch: int, max_len: int,
                  dtype: torch.dtype = torch.float16, device: str | torch.device = "cuda") -> None:
-        if dtype != torch.bfloat16:
-            raise ValueError(f"the qweninfer_b200 KV cache is bfloat16 (the model dtype); got {dtype}")
+        # The kernels read and write a bfloat16 cache (the reference's cache dtype for a
+        # bf16 model). A float16 or float32 request (the reference's default is float16)
+        # gets the same bfloat16 storage: `dtype` is accepted for API compatibility.
+        if dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise ValueError(f"KV cache dtype must be bfloat16, float16 or float32; got {dtype}")
         shape = (cfg.num_hidden_layers, max_batch, cfg.num_key_value_heads, max_len, cfg.head_dim)
-        self.k = torch.zeros(shape, dtype=dtype, device=device)
-        self.v = torch.zeros(shape, dtype=dtype, device=device)
+        self.k = torch.zeros(shape, dtype=torch.bfloat16, device=device)
+        self.v = torch.zeros(shape, dtype=torch.bfloat16, device=device)
         self.max_batch = max_batch
         self.max_len = max_len
         self.window = 0

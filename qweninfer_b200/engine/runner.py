@@ -18,7 +18,7 @@ import torch
 
 from qweninfer_b200 import _lib
 from qweninfer_b200.engine.kv_cache import KVCache
-from qweninfer_b200.models.qwen2 import PersistentPlan, use_persistent
+from qweninfer_b200.models.qwen2 import use_step
 
 
 class _Staging:
@@ -63,30 +63,26 @@ class DecodeRunner:
         self.d_slots = torch.zeros(max_batch, dtype=torch.int64, device=self.dev)
         self.h_slots_np = self.h_slots.numpy()
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
-        self.plans: dict[tuple, PersistentPlan] = {}
-        self.plan_host = PersistentPlan.host_buffer()
         self.done = torch.cuda.Event()
         self.steps = 0
         # accounting for benchmarks: kernels launched and bytes moved host<->device
         self.launches = 0
         self.h2d_bytes = 0
         self.d2h_bytes = 0
-        self.kernels_per_forward = lambda M: 1 if use_persistent(M) else 1 + 5 * model.cfg.num_hidden_layers + 1
+        self.kernels_per_forward = lambda M: 1 + 5 * model.cfg.num_hidden_layers + 1
 
     # ------------------------------------------------------------ helpers
 
-    def _forward(self, st: _Staging, M: int, ws, head_lo: int, n_head: int) -> None:
-        self.launches += self.kernels_per_forward(M)
-        if use_persistent(M):
-            # one cooperative launch; the stage table for these fixed buffers is planned once
-            key = (id(st), M, head_lo, id(ws))
-            plan = self.plans.get(key)
-            if plan is None:
-                plan = PersistentPlan(self.model, self.cache, ws, st.ptr(0), st.ptr(1), st.ptr(2), M, head_lo, 1,
-                                      n_head, None, 0, 0, self.d_slots.data_ptr(), self.plan_host)
-                self.plans[key] = plan
-            plan.launch()
+    def _forward(self, st: _Staging, M: int, ws, head_lo: int, n_head: int, decode: bool = False) -> None:
+        if decode and use_step(M):
+            # the whole step (embedding, every layer, head + argmax) as one launch
+            self.launches += 1
+            _lib.check(_lib.lib().qi_decode_step(
+                C.byref(self.model.native()), C.byref(self.cache.native()), C.byref(ws.struct),
+                st.ptr(0), st.ptr(1), st.ptr(2), M, None, 0, 0, self.d_slots.data_ptr(),
+                _lib.stream_ptr(self.dev)), "qi_decode_step")
             return
+        self.launches += self.kernels_per_forward(M)
         _lib.check(_lib.lib().qi_forward(
             C.byref(self.model.native()), C.byref(self.cache.native()), C.byref(ws.struct),
             st.ptr(0), st.ptr(1), st.ptr(2), M, head_lo, 1, n_head, None, 0, 0,
@@ -180,11 +176,11 @@ class DecodeRunner:
             g.replay()
         else:
             self.ws.plan(B)
-            self._forward(self.dec, B, self.ws, 0, B)
+            self._forward(self.dec, B, self.ws, 0, B, decode=True)
             if self.cuda_graphs:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
-                    self._forward(self.dec, B, self.ws, 0, B)
+                    self._forward(self.dec, B, self.ws, 0, B, decode=True)
                 self.graphs[B] = g
         self.steps += 1
         return self._read(B)

@@ -104,6 +104,14 @@ def build_rope_cache(head_dim: int, max_seq_len: int, theta: float,
     return emb.cos(), emb.sin()
 
 
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    """qwen2.py:76-83: for the half-split pairs (x[i], x[i + half]) return
+    (-x[i + half], x[i]). A tensor helper of the API: the kernels rotate inside the QKV
+    epilogue (and qi_rope) and never call it."""
+    half = x.shape[-1] // 2
+    return torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+
+
 def apply_rope(q: torch.Tensor, k: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                positions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """qwen2.py:86-99: rotate q (B,H,S,hd) and k (B,Hkv,S,hd) by their positions ((S,) or
@@ -216,7 +224,8 @@ class Attention(nn.Module):
         else:
             kl, vl = _single_layer_view(cache, self.layer_idx)
             row_start, max_len = cache.row_start, cache.max_len
-        if int(pos.max()) >= max_len or int(pos.max()) >= cos.shape[0]:
+        if positions.device.type == "cpu" and (int(positions.max()) >= max_len or
+                                               int(positions.max()) >= cos.shape[0]):
             raise IndexError("position beyond the cache or RoPE table")
         M = B * S
         pos32 = pos.reshape(M).to(torch.int32).contiguous()
@@ -225,7 +234,13 @@ class Attention(nn.Module):
         q = torch.empty(M, HIDDEN, dtype=torch.float32, device=dev)
         attn = torch.empty_like(q)
         out = torch.zeros_like(q)
-        ws = _AttnScratch(M, max_len, dev)
+        # split scratch, kept per (tokens, cache length) so repeated calls allocate nothing
+        key = (M, max_len, dev)
+        ws = self._scratch.get(key) if hasattr(self, "_scratch") else None
+        if ws is None:
+            if not hasattr(self, "_scratch"):
+                self._scratch = {}
+            ws = self._scratch[key] = _AttnScratch(M, max_len, dev)
         err = ws.err
         s = _lib.stream_ptr(dev)
         L = _lib.lib()
@@ -300,45 +315,15 @@ def gate_up_tile(M: int) -> int:
     return 8 if M <= 8 else 32 if M <= 32 else 64 if M <= 384 else 128
 
 
-def use_persistent(M: int) -> bool:
-    """Whole forward as one cooperative launch for M <= 128 tokens on the tensor-core
-    path (QI_PERSISTENT=1). Off by default: its per-stage dependency chain is the same as
-    that of the per-stage launches, which measure faster."""
+STEP_MAX_TOKENS = 32
+
+
+def use_step(M: int) -> bool:
+    """A decode step of M <= 32 rows (one token per cache row) as one cooperative launch
+    (`qi_decode_step`) when QI_STEP=1; by default the per-projection launches of
+    `qi_forward`, which measure faster for now."""
     import os
-    return M <= 128 and use_tensor_cores() and os.environ.get("QI_PERSISTENT", "0") == "1"
-
-
-class PersistentPlan:
-    """Device copy of a persistent-forward stage table (qi_persistent_plan) for fixed
-    buffers; launch() enqueues the single cooperative kernel on the current stream.
-    Planning is done once per buffer configuration: it fills a pinned host buffer
-    (`host`, shared by the caller's plans), copies it to the device and waits for the copy."""
-
-    TABLE_BYTES = 256 * 1024
-
-    @staticmethod
-    def host_buffer() -> torch.Tensor:
-        return torch.empty(PersistentPlan.TABLE_BYTES, dtype=torch.uint8, pin_memory=True)
-
-    def __init__(self, model, cache, ws, ids_ptr, pos_ptr, rows_ptr, M, head_lo, head_stride, n_head,
-                 logits_ptr, logits_bf16, logits_ld, slots_ptr, host: torch.Tensor) -> None:
-        n = C.c_int(0)
-        L = _lib.lib()
-        _lib.check(L.qi_persistent_plan(
-            C.byref(model.native()), C.byref(cache.native()), C.byref(ws.struct), ids_ptr, pos_ptr, rows_ptr, M,
-            head_lo, head_stride, n_head, logits_ptr, logits_bf16, logits_ld, slots_ptr, host.data_ptr(),
-            host.numel(), C.byref(n)), "qi_persistent_plan")
-        self.n_stages = n.value
-        used = self.n_stages * L.qi_persistent_stage_bytes()
-        self.table = torch.empty(used, dtype=torch.uint8, device=model.device)
-        self.table.copy_(host[:used], non_blocking=True)
-        torch.cuda.current_stream(model.device).synchronize()  # `host` may be refilled next
-        self.ws, self.M, self.dev = ws, M, model.device
-        self._keep = (model, cache)  # the table points into their tensors
-
-    def launch(self) -> None:
-        _lib.check(_lib.lib().qi_persistent_launch(self.table.data_ptr(), self.n_stages, C.byref(self.ws.struct),
-                                                   self.M, _lib.stream_ptr(self.dev)), "qi_persistent_launch")
+    return M <= STEP_MAX_TOKENS and use_tensor_cores() and os.environ.get("QI_STEP", "0") == "1"
 
 
 def use_tensor_cores() -> bool:
@@ -367,7 +352,7 @@ class Workspace:
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         # tensor-core path: activation tiles (hi/lo bf16), sums of squares, stream-K scratch,
         # padded to whole 128-token tiles so that any projection's token tile (a power of
-        # two up to 128, tiles chosen per projection) and the persistent forward's fit
+        # two up to 128, tiles chosen per projection) and the decode step's fit
         nt = 128
         pad = -(-max_tokens // nt) * nt
         bf = dict(dtype=torch.bfloat16, device=device)
@@ -379,15 +364,14 @@ class Workspace:
         self.tc_scratch = torch.empty(sms * 2 * 128 * nt, **f32)
         n_counters = max(76 * -(-pad // 8), -(-vocab // 128), 64)  # any token tile down to 8
         self.tc_counters = torch.zeros(n_counters, dtype=torch.int32, device=device)
-        self.persist_done = torch.zeros(512 * 32, dtype=torch.int32, device=device)  # 512 stages, 128 B apart
-        self.persist_trace = torch.zeros(513, dtype=torch.int64, device=device)
+        # decode-step phase counters: one 128-byte line per phase, 1 + 6 per layer (32 layers)
+        self.step_counters = torch.zeros(32 * (1 + 6 * 32), dtype=torch.int32, device=device)
         self.struct = _lib.QiWorkspace(
             self.x.data_ptr(), self.q.data_ptr(), self.attn.data_ptr(), self.h.data_ptr(),
             self.attn_part.data_ptr(), self.attn_counters.data_ptr(), max_tokens, 1, 128, self.err.data_ptr(),
             int(use_tensor_cores()), self.act_x.data_ptr(), self.act_attn.data_ptr(), self.act_h.data_ptr(),
             self.ss.data_ptr(), pad, self.tc_scratch.data_ptr(), self.tc_scratch.numel(),
-            self.tc_counters.data_ptr(), n_counters, self.persist_done.data_ptr(), self.persist_done.numel(),
-            self.persist_trace.data_ptr())
+            self.tc_counters.data_ptr(), n_counters, self.step_counters.data_ptr(), self.step_counters.numel())
 
     def plan(self, M: int) -> "Workspace":
         self.struct.split_keys, self.struct.max_splits = _split_plan(M, self.max_len)
@@ -490,32 +474,41 @@ class Qwen2(nn.Module):
     # ------------------------------------------------------------ forward
 
     def _inputs(self, input_ids, positions, cache):
-        """Validate on the host and build the int32 (ids, positions, rows) of B*S tokens."""
+        """Build the int32 (ids, positions, rows) of B*S tokens. Inputs given on the host are
+        checked there; inputs already on the device are not read back (no host
+        synchronisation, as in the reference's forward): the kernels check every position
+        and cache row and clamp token ids, and record QI_ERR_INDEX in the workspace error
+        word (`check()`) instead of touching memory outside the cache."""
         from qweninfer_b200.engine.kv_cache import KVCache
         dev = self.device
         _lib.ensure_device(dev)
         B, S = input_ids.shape
         if positions is None:
-            positions = torch.arange(S, device=dev).expand(B, S)
+            positions = torch.arange(S).expand(B, S)
         elif positions.dim() == 1:
-            positions = positions.to(dev).expand(B, S)
-        positions = positions.to(dev)
+            positions = positions.expand(B, S)
         if cache is None:
             cache = KVCache(self.cfg, B, S, dtype=torch.bfloat16, device=dev)
-        M = B * S
-        ids = input_ids.to(dev).reshape(M)
-        pos = positions.reshape(M)
-        lo, hi = int(pos.min()), int(pos.max())
-        if lo < 0 or hi >= cache.max_len or hi >= self.rope_cos.shape[0]:
-            raise IndexError(f"positions [{lo}, {hi}] outside cache ({cache.max_len}) or RoPE table")
         if cache.row_start < 0 or cache.row_start + B > cache.max_batch:
             raise IndexError(f"rows [{cache.row_start}, {cache.row_start + B}) outside the cache")
-        if int(ids.min()) < 0 or int(ids.max()) >= self.cfg.vocab_size:
-            raise IndexError("token id outside the vocabulary")
-        ids32 = ids.to(torch.int32).contiguous()
-        pos32 = pos.to(torch.int32).contiguous()
+        M = B * S
+        if positions.device.type == "cpu":
+            lo, hi = int(positions.min()), int(positions.max())
+            if lo < 0 or hi >= cache.max_len or hi >= self.rope_cos.shape[0]:
+                raise IndexError(f"positions [{lo}, {hi}] outside cache ({cache.max_len}) or RoPE table")
+        if input_ids.device.type == "cpu":
+            if int(input_ids.min()) < 0 or int(input_ids.max()) >= self.cfg.vocab_size:
+                raise IndexError("token id outside the vocabulary")
+        ids32 = input_ids.reshape(M).to(device=dev, dtype=torch.int32, non_blocking=True).contiguous()
+        pos32 = positions.reshape(M).to(device=dev, dtype=torch.int32, non_blocking=True).contiguous()
         rows32 = (cache.row_start + torch.arange(B, device=dev, dtype=torch.int32)).repeat_interleave(S)
         return cache, M, ids32, pos32, rows32
+
+    def check(self) -> None:
+        """Raise if a kernel of this model's forwards recorded an error (an index outside
+        the cache or vocabulary, or a timed-out wait); synchronises."""
+        for ws in self._workspaces.values():
+            ws.check()
 
     @torch.inference_mode()
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor | None = None, cache=None,
@@ -525,28 +518,19 @@ class Qwen2(nn.Module):
         cache, M, ids32, pos32, rows32 = self._inputs(input_ids, positions, cache)
         # head tokens: every token, or the last of each sequence (b*S + S-1)
         n_head, head_lo, head_stride = (B, S - 1, S) if last_only else (M, 0, 1)
-        ldt = logits_dtype or self.dtype
-        if ldt not in (torch.float32, torch.bfloat16):
-            raise ValueError("logits are produced in float32 or bfloat16")
+        want = logits_dtype or getattr(self, "logits_dtype", None) or self.dtype
+        # the kernels write fp32 or bf16 logits; a float16 request is converted from fp32
+        ldt = torch.bfloat16 if want == torch.bfloat16 else torch.float32
         logits = torch.empty(n_head, self.cfg.vocab_size, dtype=ldt, device=dev)
         slots = torch.zeros(M, dtype=torch.int64, device=dev)
         ws = self.workspace(max(M, 1), cache.max_len).plan(M)
-        if use_persistent(M):
-            if getattr(self, "_plan_host", None) is None:
-                self._plan_host = PersistentPlan.host_buffer()
-            plan = PersistentPlan(self, cache, ws, ids32.data_ptr(), pos32.data_ptr(), rows32.data_ptr(), M, head_lo,
-                                  head_stride, n_head, logits.data_ptr(), int(ldt == torch.bfloat16),
-                                  self.cfg.vocab_size, slots.data_ptr(), self._plan_host)
-            plan.launch()
-            self.last_argmax = self.decode_argmax(slots[:n_head])
-            return logits.view(B, 1 if last_only else S, self.cfg.vocab_size)
         _lib.check(_lib.lib().qi_forward(
             C.byref(self.native()), C.byref(cache.native()), C.byref(ws.struct), ids32.data_ptr(),
             pos32.data_ptr(), rows32.data_ptr(), M, head_lo, head_stride, n_head, logits.data_ptr(),
             int(ldt == torch.bfloat16), self.cfg.vocab_size, slots.data_ptr(), _lib.stream_ptr(dev)),
             "qi_forward")
         self.last_argmax = self.decode_argmax(slots[:n_head])
-        return logits.view(B, 1 if last_only else S, self.cfg.vocab_size)
+        return logits.view(B, 1 if last_only else S, self.cfg.vocab_size).to(want)
 
     @torch.inference_mode()
     def residual_stream(self, input_ids: torch.Tensor, n_layers: int, positions: torch.Tensor | None = None,
@@ -586,21 +570,24 @@ class Qwen2(nn.Module):
         """qwen2.py:310-337: meta-device construction, safetensors load (strict), RoPE
         tables rebuilt in fp32, `fuse()` on the host, then one move to `device`.
 
-        The kernels hold weights in bfloat16; `dtype` must be torch.bfloat16 (the
-        checkpoint's native format). Other dtypes raise rather than silently change the
-        numerics."""
+        The kernels compute with bfloat16 weights and fp32 activations, whatever `dtype`
+        asks for (the reference's default is float16). A float16 or float32 request loads
+        the checkpoint in that dtype and rounds the weights to bfloat16 once (8 mantissa
+        bits instead of float16's 11: the weight rounding the parity bar is measured
+        against); `dtype` then only sets the dtype of the returned logits."""
         from safetensors.torch import load_file
 
-        if dtype != torch.bfloat16:
-            raise ValueError(f"qweninfer_b200 kernels use bfloat16 weights; got dtype={dtype}")
+        if dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise ValueError(f"dtype must be bfloat16, float16 or float32; got {dtype}")
         path = Path(path)
         cfg = Qwen2Config.from_json(path / "config.json")
         with torch.device("meta"):
             model = cls(cfg, max_seq_len, residual_fp32)
         state = load_file(path / "model.safetensors", device="cpu")
-        state = {k.removeprefix("model."): t.to(dtype) for k, t in state.items()}
+        state = {k.removeprefix("model."): t.to(dtype).to(torch.bfloat16) for k, t in state.items()}
         model.load_state_dict(state, strict=True, assign=True)
         model.rope_cos, model.rope_sin = build_rope_cache(cfg.head_dim, max_seq_len, cfg.rope_theta)
+        model.logits_dtype = dtype
         if fuse:
             model.fuse()
         return model.to(device).eval()

@@ -222,13 +222,11 @@ def test_serving_trace_on_gpu(gpu_model, name):
     assert g["kwargs"].get("pad_to") in (None, pad_table(64))
 
 
-@pytest.mark.parametrize("persistent", [False, True])
-def test_forward_writes_only_head_slots(gpu_model, persistent):
-    """qi_forward / the persistent launch zero and fill argmax_slots[0..n_head) only: a
-    100-token prefill with one head token must leave the rest of the buffer untouched."""
+def test_forward_writes_only_head_slots(gpu_model):
+    """qi_forward zeroes and fills argmax_slots[0..n_head) only: a 100-token prefill with
+    one head token must leave the rest of the buffer untouched."""
     import ctypes as C
     from qweninfer_b200 import _lib
-    from qweninfer_b200.models.qwen2 import PersistentPlan
     M, L = 100, _lib.lib()
     cache = KVCache(gpu_model.cfg, 1, 128, dtype=torch.bfloat16, device="cuda")
     ids = torch.randint(0, gpu_model.cfg.vocab_size, (M,), dtype=torch.int32, device="cuda")
@@ -237,18 +235,34 @@ def test_forward_writes_only_head_slots(gpu_model, persistent):
     sentinel = 0x0123456789ABCDEF
     slots = torch.full((M + 8,), sentinel, dtype=torch.int64, device="cuda")
     ws = gpu_model.workspace(M, 128).plan(M)
-    if persistent:
-        plan = PersistentPlan(gpu_model, cache, ws, ids.data_ptr(), pos.data_ptr(), rows.data_ptr(), M, M - 1, 1, 1,
-                              None, 0, 0, slots.data_ptr(), PersistentPlan.host_buffer())
-        plan.launch()
-    else:
-        _lib.check(L.qi_forward(C.byref(gpu_model.native()), C.byref(cache.native()), C.byref(ws.struct),
-                                ids.data_ptr(), pos.data_ptr(), rows.data_ptr(), M, M - 1, 1, 1, None, 0, 0,
-                                slots.data_ptr(), _lib.stream_ptr(gpu_model.device)), "qi_forward")
+    _lib.check(L.qi_forward(C.byref(gpu_model.native()), C.byref(cache.native()), C.byref(ws.struct),
+                            ids.data_ptr(), pos.data_ptr(), rows.data_ptr(), M, M - 1, 1, 1, None, 0, 0,
+                            slots.data_ptr(), _lib.stream_ptr(gpu_model.device)), "qi_forward")
     torch.cuda.synchronize()
     ws.check()
     assert int(slots[0]) != sentinel
     assert bool((slots[1:] == sentinel).all())
+
+
+def test_decode_step_writes_only_its_slots(gpu_model):
+    """qi_decode_step zeroes and fills argmax_slots[0..M) only."""
+    import ctypes as C
+    from qweninfer_b200 import _lib
+    M = 5
+    cache = KVCache(gpu_model.cfg, M, 64, dtype=torch.bfloat16, device="cuda")
+    ids = torch.randint(0, gpu_model.cfg.vocab_size, (M,), dtype=torch.int32, device="cuda")
+    pos = torch.zeros(M, dtype=torch.int32, device="cuda")
+    rows = torch.arange(M, dtype=torch.int32, device="cuda")
+    sentinel = 0x0123456789ABCDEF
+    slots = torch.full((M + 8,), sentinel, dtype=torch.int64, device="cuda")
+    ws = gpu_model.workspace(32, 64).plan(M)
+    _lib.check(_lib.lib().qi_decode_step(C.byref(gpu_model.native()), C.byref(cache.native()), C.byref(ws.struct),
+                                         ids.data_ptr(), pos.data_ptr(), rows.data_ptr(), M, None, 0, 0,
+                                         slots.data_ptr(), _lib.stream_ptr(gpu_model.device)), "qi_decode_step")
+    torch.cuda.synchronize()
+    ws.check()
+    assert bool((slots[:M] != sentinel).all())
+    assert bool((slots[M:] == sentinel).all())
 
 
 def test_prefill_many_matches_single_prefills(gpu_model):
