@@ -223,6 +223,9 @@ typedef struct {
                                   step_counters_len >= 32 * (1 + 6 * layers); zeroed by
                                   each qi_decode_step call                            */
   int step_counters_len;
+  unsigned long long* step_trace; /* optional (may be NULL): the timeline of each
+                                     qi_decode_step launch, 8 globaltimer stamps (ns) per
+                                     CTA and phase: (148 * 194 * 8) uint64 (see step.h) */
 } qi_workspace;
 
 /* Full Qwen2 forward of M tokens (qweninfer/models/qwen2.py:263-292 with a cache):

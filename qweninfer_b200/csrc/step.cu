@@ -47,6 +47,22 @@ constexpr uint32_t kSlotBytes = kSlotKB * 1024;
 constexpr int kMaxSlots = 12;
 constexpr int kPartStride = kGqa * (kHeadDim + 2);  // floats per (token, head, split) partial
 
+// The CTA's share of each projection (the same in every layer) and its ring slot count.
+struct Shares {
+  Part P[6];
+  int slots[6];
+  __device__ void init(int cta, int vocab) {
+    for (int op = 0; op < 6; ++op) {
+      if (op == kAttn) {
+        slots[op] = 0;
+        continue;
+      }
+      P[op] = part_of(op, cta, vocab);
+      slots[op] = for_each_piece(P[op], 0, [](const Piece&, int, int, bool, bool) {});
+    }
+  }
+};
+
 // The fixed part of shared memory (before the ring). At least 16 KB: the UMMA A operand of
 // a piece that starts mid-tile is addressed from below the piece (rows outside the piece
 // are read but never used), which may reach up to 15 KB before the first slot.
@@ -61,6 +77,7 @@ struct StepSmem {
   uint64_t recv_free;   // the peer has consumed my previous push (1 arrival)
   uint32_t tmem_slot;
   int alast;
+  Shares sh;                    // this CTA's share of every projection
   int tpos[kMaxTokens];
   int trow[kMaxTokens];
   float rsm[kMaxTokens];
@@ -95,18 +112,26 @@ __device__ __forceinline__ bool err_set(const int* err) {
 }
 __device__ __forceinline__ void report_index(int* err) { atomicCAS(err, 0, QI_ERR_INDEX); }
 
-// Bounded mbarrier wait that also gives up once any CTA has recorded a timeout.
+// Bounded mbarrier wait that also gives up once any CTA has recorded a timeout. The error
+// word (a global load) is only read every kErrPollNs of waiting, so a completed phase is
+// seen within one try_wait instead of behind a memory round trip.
+constexpr uint64_t kErrPollNs = 16000;
+
 __device__ __noinline__ bool swait(uint64_t* bar, uint32_t parity, int* err) {
   for (int i = 0; i < 64; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
+  uint64_t next = t0 + kErrPollNs;
   while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
-    if (err_set(err)) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      atomicExch(err, QI_ERR_TIMEOUT);
-      return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t now = global_timer_ns();
+    if (now >= next) {
+      if (err_set(err)) return false;
+      if (now - t0 > kWaitLimitNs) {
+        atomicExch(err, QI_ERR_TIMEOUT);
+        return false;
+      }
+      next = now + kErrPollNs;
     }
   }
 }
@@ -126,13 +151,17 @@ __device__ __noinline__ bool swait_cluster(uint64_t* bar, uint32_t parity, int* 
   for (int i = 0; i < 64; ++i)
     if (try_wait()) return true;
   const uint64_t t0 = global_timer_ns();
+  uint64_t next = t0 + kErrPollNs;
   while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (try_wait()) return true;
-    if (err_set(err)) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      atomicExch(err, QI_ERR_TIMEOUT);
-      return false;
+    if (try_wait()) return true;
+    const uint64_t now = global_timer_ns();
+    if (now >= next) {
+      if (err_set(err)) return false;
+      if (now - t0 > kWaitLimitNs) {
+        atomicExch(err, QI_ERR_TIMEOUT);
+        return false;
+      }
+      next = now + kErrPollNs;
     }
   }
 }
@@ -156,18 +185,51 @@ __device__ __forceinline__ void wbar() { asm volatile("bar.sync 1, 256;" ::: "me
 // named barrier of one 128-thread half of the workers (reduce units)
 __device__ __forceinline__ void hbar(int h) { asm volatile("bar.sync %0, 128;" ::"r"(2 + h) : "memory"); }
 
-// Poll a phase counter until all CTAs have added their 1 (bounded; one thread).
+// Poll a phase counter until all CTAs have added their 1 (bounded; one thread; the error
+// word is read every kErrPollNs).
 __device__ __noinline__ bool wait_phase(const unsigned* ctr, int* err) {
   if (ld_acquire_gpu(ctr) >= (unsigned)kGrid) return true;
   const uint64_t t0 = global_timer_ns();
+  uint64_t next = t0 + kErrPollNs;
   while (true) {
     if (ld_acquire_gpu(ctr) >= (unsigned)kGrid) return true;
-    if (err_set(err)) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
-      atomicExch(err, QI_ERR_TIMEOUT);
-      return false;
+    const uint64_t now = global_timer_ns();
+    if (now >= next) {
+      if (err_set(err)) return false;
+      if (now - t0 > kWaitLimitNs) {
+        atomicExch(err, QI_ERR_TIMEOUT);
+        return false;
+      }
+      next = now + kErrPollNs;
     }
   }
+}
+
+// Position in the ring of the slot sequence: ring slot `idx` in its `lap`-th use (parity
+// lap & 1); advanced slot by slot, so no division by the slot count per piece.
+struct RingPos {
+  int idx = 0;
+  uint32_t lap = 0;
+  int ns;
+  __device__ explicit RingPos(int n) : ns(n) {}
+  __device__ __forceinline__ void next() {
+    if (++idx == ns) {
+      idx = 0;
+      ++lap;
+    }
+  }
+  __device__ __forceinline__ void advance(int n) {
+    for (int i = 0; i < n; ++i) next();
+  }
+};
+
+// Timeline stamp (one thread; no effect without a trace buffer).
+__device__ __forceinline__ void stamp(const StepParams& p, int cta, int phase, int event) {
+  if (p.trace) p.trace[((long long)cta * kTracePhases + phase) * kTraceEvents + event] = global_timer_ns();
+}
+__device__ __forceinline__ int phase_of(int op, int l, int n_layers) {
+  return op == kHead ? 1 + kPhasesPerLayer * n_layers
+                     : counter_index(l, op == kQkv ? 0 : op == kO ? 2 : op == kGateUp ? 3 : 4);
 }
 
 __device__ __forceinline__ const uint16_t* weights_of(const StepParams& p, int op, int l) {
@@ -207,42 +269,52 @@ __device__ __forceinline__ int attn_slot_count(const StepParams& p, const StepSm
 
 // ------------------------------------------------------------------ producer
 
-__device__ void run_producer(const StepParams& p, StepSmem& S, uint8_t* ring, int cta, int lane) {
-  const int ns = p.slots;
-  int slot_i = 0;
-  const int n_attn = attn_slot_count(p, S, cta);
+// All 32 lanes walk the slot sequence together; the lane whose number is the ring slot
+// index waits for the slot to be free and issues its copies (one issuing lane per ring
+// slot keeps several slots' copies in flight: one thread's bulk copies are processed one
+// after another). Slots are freed in order, so walking them in order loses nothing.
+__device__ void run_producer(const StepParams& p, StepSmem& S, uint8_t* ring, int cta, int lane,
+                             const Shares& sh) {
+  RingPos rp(p.slots);
   auto gemm = [&](int op, int l) {
-    const Part P = part_of(op, cta, p.vocab);
+    const Part& P = sh.P[op];
+    if (P.empty()) return;
     const uint16_t* w = weights_of(p, op, l);
     const int KB = op_kblocks(op);
     int cur = -1;
-    const int n = for_each_piece(P, slot_i, [&](const Piece& pc, int slot, int off, bool, bool) {
-      if (slot % ns != lane) return;
+    for_each_piece(P, 0, [&](const Piece& pc, int slot, int off, bool, bool) {
       if (slot != cur) {
-        if (cur >= 0) mbar_arrive(&S.full[cur % ns]);
+        if (cur >= 0) {
+          if (lane == rp.idx) mbar_arrive(&S.full[rp.idx]);
+          rp.next();
+        }
         cur = slot;
-        if (slot >= ns) swait(&S.empty[slot % ns], (uint32_t)(((slot / ns) & 1) ^ 1), p.err);
+        if (lane == rp.idx) swait(&S.empty[rp.idx], (rp.lap & 1u) ^ 1u, p.err);
       }
-      const uint32_t bytes = (uint32_t)pc.kbytes() * 1024u;
-      const int mt = P.tile0() + pc.u;
-      mbar_expect_tx(&S.full[slot % ns], bytes);
-      bulk_g2s(ring + (size_t)(slot % ns) * kSlotBytes + (size_t)off * 1024,
-               w + ((long long)mt * KB + pc.kb) * 8192 + (long long)pc.lo * 512, bytes, &S.full[slot % ns]);
+      if (lane == rp.idx) {
+        const uint32_t bytes = (uint32_t)pc.kbytes() * 1024u;
+        const int mt = P.tile0() + pc.u;
+        mbar_expect_tx(&S.full[rp.idx], bytes);
+        bulk_g2s(ring + (size_t)rp.idx * kSlotBytes + (size_t)off * 1024,
+                 w + ((long long)mt * KB + pc.kb) * 8192 + (long long)pc.lo * 512, bytes, &S.full[rp.idx]);
+      }
     });
-    if (cur >= 0) mbar_arrive(&S.full[cur % ns]);
-    slot_i += n;
+    if (lane == rp.idx) mbar_arrive(&S.full[rp.idx]);
+    rp.next();
   };
   auto attn = [&](int l) {
     for_each_attn_unit(p, S, cta, [&](int t, int g, int, int kbeg, int kend) {
       const long long hb = p.layer_elems * l + ((long long)S.trow[t] * kKvHeads + g) * p.max_len * kHeadDim;
       for (int k0 = kbeg; k0 < kend; k0 += 128) {
         const int nk = min(128, kend - k0);
-        for (int kv = 0; kv < 2; ++kv, ++slot_i) {
-          if (slot_i % ns != lane) continue;
-          if (slot_i >= ns) swait(&S.empty[slot_i % ns], (uint32_t)(((slot_i / ns) & 1) ^ 1), p.err);
-          mbar_arrive_expect_tx(&S.full[slot_i % ns], (uint32_t)nk * kHeadDim * 2);
-          bulk_g2s(ring + (size_t)(slot_i % ns) * kSlotBytes, (kv ? p.vc : p.kc) + hb + (long long)k0 * kHeadDim,
-                   (uint32_t)nk * kHeadDim * 2, &S.full[slot_i % ns]);
+        for (int kv = 0; kv < 2; ++kv) {
+          if (lane == rp.idx) {
+            swait(&S.empty[rp.idx], (rp.lap & 1u) ^ 1u, p.err);
+            mbar_arrive_expect_tx(&S.full[rp.idx], (uint32_t)nk * kHeadDim * 2);
+            bulk_g2s(ring + (size_t)rp.idx * kSlotBytes, (kv ? p.vc : p.kc) + hb + (long long)k0 * kHeadDim,
+                     (uint32_t)nk * kHeadDim * 2, &S.full[rp.idx]);
+          }
+          rp.next();
         }
       }
     });
@@ -255,31 +327,37 @@ __device__ void run_producer(const StepParams& p, StepSmem& S, uint8_t* ring, in
     gemm(kDown, l);
   }
   gemm(kHead, 0);
-  (void)n_attn;
 }
 
 // ----------------------------------------------------------------------- MMA
 
 __device__ void run_mma(const StepParams& p, StepSmem& S, uint8_t* ring, uint8_t* bbuf, uint32_t tmem_base,
-                        int cta) {
-  const int ns = p.slots, NT = p.NT;
+                        int cta, const Shares& sh) {
+  const int NT = p.NT;
   const uint32_t idesc = idesc_bf16(128, 2 * NT);
   const uint32_t ring_a = smem_u32(ring), b_a = smem_u32(bbuf);
   const int n_attn = attn_slot_count(p, S, cta);
-  int slot_i = 0;
+  RingPos rp(p.slots);
   uint32_t units = 0, ops = 0;
+  int cur_l = 0;
   auto gemm = [&](int op) {
-    const Part P = part_of(op, cta, p.vocab);
+    const Part& P = sh.P[op];
     if (P.empty()) return;
+    const int ph = phase_of(op, cur_l, p.n_layers);
     swait(&S.b_full, ops & 1u, p.err);
+    stamp(p, cta, ph, kTrMmaB);
     tc_fence_after();
+    bool first_unit = true;
     int cur = -1;
     uint32_t b = 0;
-    const int n = for_each_piece(P, slot_i, [&](const Piece& pc, int slot, int off, bool first, bool last) {
+    for_each_piece(P, 0, [&](const Piece& pc, int slot, int off, bool first, bool last) {
       if (slot != cur) {
-        if (cur >= 0) umma_commit(&S.empty[cur % ns]);
+        if (cur >= 0) {
+          umma_commit(&S.empty[rp.idx]);
+          rp.next();
+        }
         cur = slot;
-        swait(&S.full[slot % ns], (uint32_t)((slot / ns) & 1), p.err);
+        swait(&S.full[rp.idx], rp.lap & 1u, p.err);
         tc_fence_after();
       }
       if (first) {
@@ -289,7 +367,7 @@ __device__ void run_mma(const StepParams& p, StepSmem& S, uint8_t* ring, uint8_t
       }
       const uint32_t d = tmem_base + b * 4u * (uint32_t)NT + (P.tile_major ? 0u : (uint32_t)pc.u * 2u * (uint32_t)NT);
       // row 0 of the piece's tile (rows outside the piece are read but not used)
-      const int a_off = (slot % ns) * (int)kSlotBytes + (off - pc.lo) * 1024;
+      const int a_off = rp.idx * (int)kSlotBytes + (off - pc.lo) * 1024;
       const uint32_t a0 = (uint32_t)((int)ring_a + a_off);
       const uint32_t b0 = b_a + (uint32_t)(pc.kb - P.kb0) * (uint32_t)NT * 256u;
 #pragma unroll
@@ -297,18 +375,21 @@ __device__ void run_mma(const StepParams& p, StepSmem& S, uint8_t* ring, uint8_t
         umma_bf16(d, kmajor_desc(a0 + kk * 256), kmajor_desc(b0 + kk * 256), idesc,
                   (pc.kb > P.kb0 || kk > 0) ? 1u : 0u);
       if (last) {
+        if (first_unit) stamp(p, cta, ph, kTrMmaLast);
+        first_unit = false;
         umma_commit(&S.acc_full[b]);
         ++units;
       }
     });
-    if (cur >= 0) umma_commit(&S.empty[cur % ns]);
+    umma_commit(&S.empty[rp.idx]);
+    rp.next();
     umma_commit(&S.b_empty);
     ++ops;
-    slot_i += n;
   };
   for (int l = 0; l < p.n_layers; ++l) {
+    cur_l = l;
     gemm(kQkv);
-    slot_i += n_attn;  // K/V slots: consumed by the workers
+    rp.advance(n_attn);  // K/V slots: consumed by the workers
     gemm(kO);
     gemm(kGateUp);
     gemm(kDown);
@@ -732,9 +813,8 @@ struct Worker {
   // One projection phase of this CTA: activation tiles in, accumulation unit(s), the
   // pair exchange and the fused epilogue (or the down partials).
   __device__ void gemm_phase(int op, int l, int dep) {
-    const Part P = part_of(op, cta, p.vocab);
-    const int n_slots = for_each_piece(P, 0, [](const Piece&, int, int, bool, bool) {});
-    slot_i += n_slots;
+    const Part& P = S.sh.P[op];
+    slot_i += S.sh.slots[op];
     const int M = p.M, NT = p.NT;
     const int nch = (M + 7) / 8;
     if (P.empty()) {
@@ -743,8 +823,11 @@ struct Worker {
     }
     const int nkb = P.kb1 - P.kb0;
     const uint16_t* act = op == kO ? p.act_attn : op == kDown ? p.act_h : p.act_x;
+    const int ph = phase_of(op, l, p.n_layers);
     if (wt == 0) {
+      stamp(p, cta, ph, kTrEnter);
       wait_phase(p.ctr + (size_t)dep * kCounterStride, p.err);
+      stamp(p, cta, ph, kTrInputs);
       fence_proxy_async_global();
       swait(&S.b_empty, (ops & 1u) ^ 1u, p.err);
       mbar_arrive_expect_tx(&S.b_full, (uint32_t)(nkb * NT * 256));
@@ -780,6 +863,7 @@ struct Worker {
     for (int uu = 0; uu < nu; ++uu) {
       const uint32_t b = units & 1u;
       swait(&S.acc_full[b], (units >> 1) & 1u, p.err);
+      if (wt == 0 && uu == 0) stamp(p, cta, ph, kTrAcc);
       tc_fence_after();
       const int v_lo = P.tile_major ? uu : 0, v_hi = P.tile_major ? uu + 1 : nt;
       for (int v = v_lo; v < v_hi; ++v) {
@@ -816,9 +900,11 @@ struct Worker {
             }
           }
           mbar_arrive_remote(map_rank(&S.recv_full, peer));
+          if (wt == 0 && uu == 0) stamp(p, cta, ph, kTrPushed);
           ++pushes;
         } else {
           swait_cluster(&S.recv_full, recvs & 1u, p.err);
+          if (wt == 0 && uu == 0) stamp(p, cta, ph, kTrRecv);
           if (op == kO) did_o_finish = true;
           for (int c = half; c < nch; c += 2) {
             float val[8];
@@ -867,17 +953,23 @@ struct Worker {
       wbar();
       if (wt < M && S.abest[wt]) atomicMax(&p.argmax[wt], S.abest[wt]);
     }
+    if (wt == 0) stamp(p, cta, ph, kTrDone);
     ++ops;
   }
 
   __device__ void run() {
+    if (wt == 0) stamp(p, cta, 0, kTrEnter);
     reduce_phase(-1);  // embedding
+    if (wt == 0) stamp(p, cta, 0, kTrDone);
     signal(0);
     for (int l = 0; l < p.n_layers; ++l) {
       gemm_phase(kQkv, l, l == 0 ? 0 : counter_index(l - 1, 5));
       signal(counter_index(l, 0));
+      if (wt == 0) stamp(p, cta, counter_index(l, 1), kTrEnter);
       wait_for(counter_index(l, 0));
+      if (wt == 0) stamp(p, cta, counter_index(l, 1), kTrInputs);
       attention_phase(l);
+      if (wt == 0) stamp(p, cta, counter_index(l, 1), kTrDone);
       signal(counter_index(l, 1));
       gemm_phase(kO, l, counter_index(l, 1));
       signal(counter_index(l, 2));
@@ -885,8 +977,11 @@ struct Worker {
       signal(counter_index(l, 3));
       gemm_phase(kDown, l, counter_index(l, 3));
       signal(counter_index(l, 4));
+      if (wt == 0) stamp(p, cta, counter_index(l, 5), kTrEnter);
       wait_for(counter_index(l, 4));
+      if (wt == 0) stamp(p, cta, counter_index(l, 5), kTrInputs);
       reduce_phase(l);
+      if (wt == 0) stamp(p, cta, counter_index(l, 5), kTrDone);
       signal(counter_index(l, 5));
     }
     gemm_phase(kHead, 0, counter_index(p.n_layers - 1, 5));
@@ -916,6 +1011,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     mbar_init(&S.recv_free, 1);
     fence_barrier_init();
   }
+  if (threadIdx.x == 32) S.sh.init(cta, p.vocab);
   if (threadIdx.x < kMaxTokens) {
     const int t = threadIdx.x;
     S.tpos[t] = t < p.M ? p.pos[t] : 0;
@@ -935,10 +1031,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
   cluster_wait();
 
   if (warp == 0) {
-    if (lane < p.slots) run_producer(p, S, ring, cta, lane);
+    run_producer(p, S, ring, cta, lane, S.sh);
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) run_mma(p, S, ring, bbuf, tmem_base, cta);
+    if (lane == 0) run_mma(p, S, ring, bbuf, tmem_base, cta, S.sh);
     __syncwarp();
   } else {
     Worker w(p, S, ring, bbuf, tmem_base, cta, threadIdx.x - 64);

@@ -56,8 +56,25 @@ struct StepParams {
   long long logits_ld;
   unsigned long long* argmax;  // (M) packed argmax slots
   int* err;
+  unsigned long long* trace;  // optional per-CTA phase timestamps (kTraceEvents per phase), or null
   int slots;           // ring slots
   uint32_t tmem_cols;
+};
+
+// Optional timeline of a launch (StepParams::trace): globaltimer stamps (ns) at
+// trace[(cta * kTracePhases + phase) * kTraceEvents + event], phase 0 = embedding,
+// 1 + 6 l + {0 qkv, 1 attention, 2 o, 3 gate/up, 4 down, 5 reduce}, 1 + 6 layers = head.
+constexpr int kTracePhases = 1 + step::kPhasesPerLayer * step::kMaxLayers + 1;
+constexpr int kTraceEvents = 8;
+enum StepTraceEvent : int {
+  kTrEnter = 0,     // the workers start the phase
+  kTrInputs = 1,    // its inputs are complete (phase counter reached)
+  kTrAcc = 2,       // the first accumulator is complete (projections)
+  kTrDone = 3,      // the phase's outputs are written (before the counter increment)
+  kTrMmaB = 4,      // MMA thread: the activation tiles have landed
+  kTrMmaLast = 5,   // MMA thread: the first unit's last UMMA is issued
+  kTrRecv = 6,      // finishing rank: the peer's partial has arrived
+  kTrPushed = 7,    // pushing rank: its partial is pushed
 };
 
 // Shared memory of one step CTA for token tile NT, and its ring slot count.

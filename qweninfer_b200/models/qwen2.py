@@ -371,7 +371,19 @@ class Workspace:
             self.attn_part.data_ptr(), self.attn_counters.data_ptr(), max_tokens, 1, 128, self.err.data_ptr(),
             int(use_tensor_cores()), self.act_x.data_ptr(), self.act_attn.data_ptr(), self.act_h.data_ptr(),
             self.ss.data_ptr(), pad, self.tc_scratch.data_ptr(), self.tc_scratch.numel(),
-            self.tc_counters.data_ptr(), n_counters, self.step_counters.data_ptr(), self.step_counters.numel())
+            self.tc_counters.data_ptr(), n_counters, self.step_counters.data_ptr(), self.step_counters.numel(),
+            None)
+
+    def trace_steps(self, on: bool = True) -> torch.Tensor | None:
+        """Record the timeline of every following qi_decode_step launch on this workspace
+        (globaltimer stamps per CTA and phase, see csrc/step.h); returns the buffer."""
+        if on:
+            if getattr(self, "step_trace", None) is None:
+                self.step_trace = torch.zeros(148 * 194 * 8, dtype=torch.int64, device=self.x.device)
+            self.struct.step_trace = self.step_trace.data_ptr()
+            return self.step_trace
+        self.struct.step_trace = None
+        return None
 
     def plan(self, M: int) -> "Workspace":
         self.struct.split_keys, self.struct.max_splits = _split_plan(M, self.max_len)
