@@ -555,7 +555,8 @@ int qi_decode_step(const qi_model* model, const qi_cache* cache, const qi_worksp
   P.err = ws->err;
   P.trace = ws->step_trace;
   P.slots = step_ring_slots(NT);
-  P.tmem_cols = NT <= 8 ? 64 : NT <= 16 ? 128 : 256;
+  P.chains = step_chains(NT);
+  P.tmem_cols = step_tmem_cols(NT);
   return rc(launch_step(P, as_stream(stream)));
 }
 

@@ -4,7 +4,7 @@
 // Why one launch: a decode step is ~120 dependent projections and attention passes over
 // 0.99 GB of weights. Launched one by one, each pays its own ramp-up, first-byte latency
 // and drain, far more than its share of the ~150 us weight stream. Here 148 resident CTAs
-// (one per SM, clusters of 2) walk the same fixed program and:
+// (one per SM) walk the same fixed program and:
 //
 //  * stream their weight pieces (step_plan.h) through a ring of shared-memory slots, one
 //    issuing lane per slot, in program order. Weights do not depend on activations, so
@@ -15,10 +15,11 @@
 //    its outputs of a phase; the waiting CTA polls for 148 with acquire semantics), then
 //    bulk-copy the activation tiles they multiply (UMMA B operand, hi/lo bf16 halves);
 //  * multiply with tcgen05 UMMAs (M = 128 weight rows, N = 2 x token tile, K = 16) into
-//    TMEM accumulators; the two CTAs of a pair hold the two k halves of the same rows and
-//    one of them adds the other's partial, received over distributed shared memory, and
-//    runs the fused epilogue (RMSNorm scale, bias + RoPE + KV append, residual + next
-//    norm operands, SwiGLU, logits + argmax).
+//    TMEM accumulators, consecutive k blocks into independent accumulator chains (one
+//    chain's UMMAs wait on each other, ~170 ns apiece at these shapes); every CTA owns
+//    whole output rows over all of K (the down projection excepted), so it runs the fused
+//    epilogue itself (RMSNorm scale, bias + RoPE + KV append, residual + next norm
+//    operands, SwiGLU, logits + argmax) with no partial sums crossing CTAs.
 //
 // Phases per layer: QKV -> attention -> o -> gate/up -> down (partials over 21 k ranges)
 // -> reduce (sum the down partials + residual, next norm operands). The embedding is a
@@ -73,8 +74,6 @@ struct StepSmem {
   uint64_t acc_empty[2];
   uint64_t b_full;
   uint64_t b_empty;
-  uint64_t recv_full;   // the peer's partial has arrived (all its 256 workers arrive)
-  uint64_t recv_free;   // the peer has consumed my previous push (1 arrival)
   uint32_t tmem_slot;
   int alast;
   Shares sh;                    // this CTA's share of every projection
@@ -88,18 +87,21 @@ struct StepSmem {
   alignas(16) float aq[kGqa * 2 * 8 * 4];   // q of the 7 heads, scaled, [head][half][chunk][4]
   alignas(16) float ap[4][32][8];           // probabilities per key group
   alignas(16) float acmb[4][kGqa][kHeadDim + 2];
-  // the peer's partial: [token / 4][128 rows][token % 4] (16-byte stores and loads)
-  alignas(16) float recv[kMaxTokens / 4][128][4];
 };
 static_assert(offsetof(StepSmem, aq) % 16 == 0 && offsetof(StepSmem, ap) % 16 == 0 &&
-                  offsetof(StepSmem, recv) % 16 == 0 && offsetof(StepSmem, abest) % 8 == 0,
+                  offsetof(StepSmem, abest) % 8 == 0,
               "vector-accessed shared arrays are aligned");
-constexpr size_t kFixedBytes = (sizeof(StepSmem) + 1023) / 1024 * 1024;
-static_assert(kFixedBytes >= 16 * 1024, "room below the ring for mid-tile piece operands");
+// >= 16 KB: the UMMA A operand of a piece that starts mid-tile is addressed from below the
+// piece (rows outside the piece are read, never used), up to 15 KB before the first slot
+constexpr size_t kFixedBytes = ((sizeof(StepSmem) + 1023) / 1024 * 1024) < 16384
+                                   ? 16384
+                                   : (sizeof(StepSmem) + 1023) / 1024 * 1024;
 
+// The activation tiles of a whole K = 896 (14 k blocks of NT tokens, hi/lo); >= 16 KB so
+// that operand rows read past the last ring slot stay inside shared memory.
 __host__ __device__ inline uint32_t b_region_bytes(int NT) {
-  const uint32_t b = 7u * (uint32_t)NT * 256u;
-  return b < 16384u ? 16384u : b;  // >= 16 KB: operand rows read past the last slot stay inside
+  const uint32_t b = 14u * (uint32_t)NT * 256u;
+  return b < 16384u ? 16384u : b;
 }
 
 // ------------------------------------------------------------------ helpers
@@ -124,36 +126,6 @@ __device__ __noinline__ bool swait(uint64_t* bar, uint32_t parity, int* err) {
   uint64_t next = t0 + kErrPollNs;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t now = global_timer_ns();
-    if (now >= next) {
-      if (err_set(err)) return false;
-      if (now - t0 > kWaitLimitNs) {
-        atomicExch(err, QI_ERR_TIMEOUT);
-        return false;
-      }
-      next = now + kErrPollNs;
-    }
-  }
-}
-
-__device__ __noinline__ bool swait_cluster(uint64_t* bar, uint32_t parity, int* err) {
-  auto try_wait = [&]() {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-  };
-  for (int i = 0; i < 64; ++i)
-    if (try_wait()) return true;
-  const uint64_t t0 = global_timer_ns();
-  uint64_t next = t0 + kErrPollNs;
-  while (true) {
-    if (try_wait()) return true;
     const uint64_t now = global_timer_ns();
     if (now >= next) {
       if (err_set(err)) return false;
@@ -269,13 +241,19 @@ __device__ __forceinline__ int attn_slot_count(const StepParams& p, const StepSm
 
 // ------------------------------------------------------------------ producer
 
-// All 32 lanes walk the slot sequence together; the lane whose number is the ring slot
-// index waits for the slot to be free and issues its copies (one issuing lane per ring
-// slot keeps several slots' copies in flight: one thread's bulk copies are processed one
-// after another). Slots are freed in order, so walking them in order loses nothing.
+// The producer warp walks the slot sequence in order. Lane 0 alone waits until a ring slot
+// is free and posts the bytes each piece will bring; after a __syncwarp the piece's 1 KB
+// groups are copied by up to 16 lanes at once (one thread's bulk copies are processed one
+// after another, so spreading a slot over lanes keeps several copies in flight). No lane
+// ever waits inside a branch the others skipped. Slots are freed in order, so walking them
+// in order loses nothing.
 __device__ void run_producer(const StepParams& p, StepSmem& S, uint8_t* ring, int cta, int lane,
                              const Shares& sh) {
   RingPos rp(p.slots);
+  auto open_slot = [&]() {
+    if (lane == 0) swait(&S.empty[rp.idx], (rp.lap & 1u) ^ 1u, p.err);
+    __syncwarp();
+  };
   auto gemm = [&](int op, int l) {
     const Part& P = sh.P[op];
     if (P.empty()) return;
@@ -285,21 +263,22 @@ __device__ void run_producer(const StepParams& p, StepSmem& S, uint8_t* ring, in
     for_each_piece(P, 0, [&](const Piece& pc, int slot, int off, bool, bool) {
       if (slot != cur) {
         if (cur >= 0) {
-          if (lane == rp.idx) mbar_arrive(&S.full[rp.idx]);
+          if (lane == 0) mbar_arrive(&S.full[rp.idx]);
           rp.next();
         }
         cur = slot;
-        if (lane == rp.idx) swait(&S.empty[rp.idx], (rp.lap & 1u) ^ 1u, p.err);
+        open_slot();
       }
-      if (lane == rp.idx) {
-        const uint32_t bytes = (uint32_t)pc.kbytes() * 1024u;
+      const int n = pc.kbytes();  // 1 KB groups
+      if (lane == 0) mbar_expect_tx(&S.full[rp.idx], (uint32_t)n * 1024u);
+      __syncwarp();
+      if (lane < n) {
         const int mt = P.tile0() + pc.u;
-        mbar_expect_tx(&S.full[rp.idx], bytes);
-        bulk_g2s(ring + (size_t)rp.idx * kSlotBytes + (size_t)off * 1024,
-                 w + ((long long)mt * KB + pc.kb) * 8192 + (long long)pc.lo * 512, bytes, &S.full[rp.idx]);
+        bulk_g2s(ring + (size_t)rp.idx * kSlotBytes + (size_t)(off + lane) * 1024,
+                 w + ((long long)mt * KB + pc.kb) * 8192 + (long long)(pc.lo + lane) * 512, 1024u, &S.full[rp.idx]);
       }
     });
-    if (lane == rp.idx) mbar_arrive(&S.full[rp.idx]);
+    if (lane == 0) mbar_arrive(&S.full[rp.idx]);
     rp.next();
   };
   auto attn = [&](int l) {
@@ -308,11 +287,16 @@ __device__ void run_producer(const StepParams& p, StepSmem& S, uint8_t* ring, in
       for (int k0 = kbeg; k0 < kend; k0 += 128) {
         const int nk = min(128, kend - k0);
         for (int kv = 0; kv < 2; ++kv) {
-          if (lane == rp.idx) {
-            swait(&S.empty[rp.idx], (rp.lap & 1u) ^ 1u, p.err);
-            mbar_arrive_expect_tx(&S.full[rp.idx], (uint32_t)nk * kHeadDim * 2);
-            bulk_g2s(ring + (size_t)rp.idx * kSlotBytes, (kv ? p.vc : p.kc) + hb + (long long)k0 * kHeadDim,
-                     (uint32_t)nk * kHeadDim * 2, &S.full[rp.idx]);
+          open_slot();
+          if (lane == 0) mbar_arrive_expect_tx(&S.full[rp.idx], (uint32_t)nk * kHeadDim * 2);
+          __syncwarp();
+          // 8 keys (1 KB) per lane
+          const int k8 = lane * 8;
+          if (k8 < nk) {
+            const int nkl = min(8, nk - k8);
+            bulk_g2s(ring + (size_t)rp.idx * kSlotBytes + (size_t)k8 * kHeadDim * 2,
+                     (kv ? p.vc : p.kc) + hb + (long long)(k0 + k8) * kHeadDim, (uint32_t)nkl * kHeadDim * 2,
+                     &S.full[rp.idx]);
           }
           rp.next();
         }
@@ -331,14 +315,23 @@ __device__ void run_producer(const StepParams& p, StepSmem& S, uint8_t* ring, in
 
 // ----------------------------------------------------------------------- MMA
 
+// Accumulators: the UMMAs of consecutive k blocks go to `chains` independent accumulators
+// (k block kb -> chain (kb - kb0) % chains) so that they do not wait on one another; the
+// epilogue adds the chains in order. A layer projection's unit (<= 2 tiles) takes TMEM
+// columns [0, 2 * chains * 2NT); the head's one-tile units alternate between buffer 0
+// (columns of tile 0) and buffer 1 (columns of tile 1), so a tile's epilogue overlaps the
+// next tile's UMMAs. Per buffer, acc_full / acc_empty count its uses.
+__device__ __forceinline__ uint32_t tile_cols(const StepParams& p) { return (uint32_t)p.chains * 2u * (uint32_t)p.NT; }
+
 __device__ void run_mma(const StepParams& p, StepSmem& S, uint8_t* ring, uint8_t* bbuf, uint32_t tmem_base,
                         int cta, const Shares& sh) {
-  const int NT = p.NT;
+  const int NT = p.NT, CH = p.chains;
   const uint32_t idesc = idesc_bf16(128, 2 * NT);
   const uint32_t ring_a = smem_u32(ring), b_a = smem_u32(bbuf);
+  const uint32_t tcols = tile_cols(p);
   const int n_attn = attn_slot_count(p, S, cta);
   RingPos rp(p.slots);
-  uint32_t units = 0, ops = 0;
+  uint32_t use0 = 0, use1 = 0, ops = 0;  // uses of accumulator buffer 0 / 1
   int cur_l = 0;
   auto gemm = [&](int op) {
     const Part& P = sh.P[op];
@@ -349,7 +342,7 @@ __device__ void run_mma(const StepParams& p, StepSmem& S, uint8_t* ring, uint8_t
     tc_fence_after();
     bool first_unit = true;
     int cur = -1;
-    uint32_t b = 0;
+    uint32_t b = 0, head_units = 0;
     for_each_piece(P, 0, [&](const Piece& pc, int slot, int off, bool first, bool last) {
       if (slot != cur) {
         if (cur >= 0) {
@@ -361,24 +354,24 @@ __device__ void run_mma(const StepParams& p, StepSmem& S, uint8_t* ring, uint8_t
         tc_fence_after();
       }
       if (first) {
-        b = units & 1u;
-        swait(&S.acc_empty[b], ((units >> 1) & 1u) ^ 1u, p.err);
+        b = P.tile_major ? (head_units & 1u) : 0u;
+        swait(&S.acc_empty[b], ((b ? use1 : use0) & 1u) ^ 1u, p.err);
         tc_fence_after();
       }
-      const uint32_t d = tmem_base + b * 4u * (uint32_t)NT + (P.tile_major ? 0u : (uint32_t)pc.u * 2u * (uint32_t)NT);
+      const int kr = pc.kb - P.kb0;
+      const uint32_t d = tmem_base + (P.tile_major ? b : (uint32_t)pc.u) * tcols +
+                         (uint32_t)(kr & (CH - 1)) * 2u * (uint32_t)NT;
       // row 0 of the piece's tile (rows outside the piece are read but not used)
       const int a_off = rp.idx * (int)kSlotBytes + (off - pc.lo) * 1024;
       const uint32_t a0 = (uint32_t)((int)ring_a + a_off);
-      const uint32_t b0 = b_a + (uint32_t)(pc.kb - P.kb0) * (uint32_t)NT * 256u;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        umma_bf16(d, kmajor_desc(a0 + kk * 256), kmajor_desc(b0 + kk * 256), idesc,
-                  (pc.kb > P.kb0 || kk > 0) ? 1u : 0u);
+      const uint32_t b0 = b_a + (uint32_t)kr * (uint32_t)NT * 256u;
+      umma_bf16_kblock(d, kmajor_desc(a0), kmajor_desc(b0), idesc, kr >= CH ? 1u : 0u);
       if (last) {
         if (first_unit) stamp(p, cta, ph, kTrMmaLast);
         first_unit = false;
         umma_commit(&S.acc_full[b]);
-        ++units;
+        if (b) ++use1; else ++use0;
+        ++head_units;
       }
     });
     umma_commit(&S.empty[rp.idx]);
@@ -406,14 +399,11 @@ struct Worker {
   uint8_t* bbuf;
   uint32_t tmem_base;
   int cta, wt, ww, lane;
-  uint32_t rank, peer;
   int slot_i = 0;
-  uint32_t units = 0, ops = 0, pushes = 0, recvs = 0;
+  uint32_t use0 = 0, use1 = 0, ops = 0;  // uses of accumulator buffer 0 / 1
 
   __device__ Worker(const StepParams& p_, StepSmem& S_, uint8_t* ring_, uint8_t* bbuf_, uint32_t tb, int cta_, int wt_)
       : p(p_), S(S_), ring(ring_), bbuf(bbuf_), tmem_base(tb), cta(cta_), wt(wt_), ww(wt_ >> 5), lane(wt_ & 31) {
-    rank = cluster_rank();
-    peer = rank ^ 1u;
   }
 
   __device__ void signal(int idx) {
@@ -458,8 +448,11 @@ struct Worker {
         } else {
           v = __ldcg(p.x + (long long)t * kHidden + f);
           float acc = 0.f;
-#pragma unroll 7
-          for (int j = 0; j < kDownRanges; ++j) acc += __ldcg(p.dpart + ((long long)j * NT + t) * kHidden + f);
+          float part[kDownRanges];  // all loads in flight, then added in k order
+#pragma unroll
+          for (int j = 0; j < kDownRanges; ++j) part[j] = __ldcg(p.dpart + ((long long)j * NT + t) * kHidden + f);
+#pragma unroll
+          for (int j = 0; j < kDownRanges; ++j) acc += part[j];
           v += acc;
         }
         p.x[(long long)t * kHidden + f] = v;
@@ -705,13 +698,19 @@ struct Worker {
 
   // ------------------------------------------------------------ projections
 
-  // Accumulator columns [8 tokens of chunk c] of this warp's 32 rows, hi + lo summed.
-  __device__ __forceinline__ void tmem_chunk(uint32_t t_base, int c, float (&v)[8]) {
-    float a[8], b[8];
-    tmem_ld8(t_base + (uint32_t)(c * 8), a);
-    tmem_ld8(t_base + (uint32_t)(p.NT + c * 8), b);
+  // Accumulator columns [8 tokens of chunk c] of this warp's 32 rows: hi + lo of every
+  // chain that received a k block, added chain by chain (a fixed order).
+  __device__ __forceinline__ void tmem_chunk(uint32_t t_tile, int c, int nchains, float (&v)[8]) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = a[i] + b[i];
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    for (int ch = 0; ch < nchains; ++ch) {
+      float a[8], b[8];
+      const uint32_t t = t_tile + (uint32_t)(ch * 2 * p.NT + c * 8);
+      tmem_ld8(t, a);
+      tmem_ld8(t + (uint32_t)p.NT, b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] += a[i] + b[i];
+    }
   }
 
   // Fused epilogue of weight row n (valid) for tokens c*8 .. c*8+nlive-1.
@@ -819,6 +818,7 @@ struct Worker {
     const int nch = (M + 7) / 8;
     if (P.empty()) {
       wait_for(dep);  // keep the phase order (nothing to multiply here)
+      if (op == kO && wt < M) p.ss_o[cta * NT + wt] = 0.f;
       return;
     }
     const int nkb = P.kb1 - P.kb0;
@@ -859,10 +859,17 @@ struct Worker {
     const int quad = (ww + 2) & 3, half = ww >> 2;
     const int row = quad * 32 + lane;
     const int nt = P.ntiles(), nu = units_of(P);
-    bool did_o_finish = false;
+    const int nchains = min(p.chains, nkb);
+    const uint32_t tcols = tile_cols(p);
+    if (op == kO) {
+      // per lane quadrant, this CTA's share of each token's sum of squares (accumulated
+      // over its tiles; each (quadrant, token) entry belongs to one warp)
+      if (wt < 4 * kMaxTokens) S.red[wt / kMaxTokens][wt % kMaxTokens] = 0.f;
+      wbar();
+    }
     for (int uu = 0; uu < nu; ++uu) {
-      const uint32_t b = units & 1u;
-      swait(&S.acc_full[b], (units >> 1) & 1u, p.err);
+      const uint32_t b = P.tile_major ? (uint32_t)(uu & 1) : 0u;
+      swait(&S.acc_full[b], (b ? use1 : use0) & 1u, p.err);
       if (wt == 0 && uu == 0) stamp(p, cta, ph, kTrAcc);
       tc_fence_after();
       const int v_lo = P.tile_major ? uu : 0, v_hi = P.tile_major ? uu + 1 : nt;
@@ -871,83 +878,41 @@ struct Worker {
         const int r_lo = 8 * (P.seg_lo(v) - 16 * mt), r_hi = 8 * (P.seg_hi(v) - 16 * mt);
         const bool valid = row >= r_lo && row < r_hi;
         const int n = mt * 128 + row;
-        const uint32_t t_base = tmem_base + ((uint32_t)(quad * 32) << 16) + b * 4u * (uint32_t)NT +
-                                (P.tile_major ? 0u : (uint32_t)v * 2u * (uint32_t)NT);
-        if (op == kDown) {
-          const int j = cta % kDownRanges;
-          for (int c = half; c < nch; c += 2) {
-            float val[8];
-            tmem_chunk(t_base, c, val);
-            const int nlive = min(8, M - c * 8);
+        const uint32_t t_tile =
+            tmem_base + ((uint32_t)(quad * 32) << 16) + (P.tile_major ? b : (uint32_t)v) * tcols;
+        for (int c = half; c < nch; c += 2) {
+          float val[8];
+          tmem_chunk(t_tile, c, nchains, val);
+          const int nlive = min(8, M - c * 8);
+          if (op == kDown) {
+            const int j = cta % kDownRanges;
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               if (i < nlive) p.dpart[((long long)j * NT + c * 8 + i) * kHidden + n] = val[i];
+            continue;
           }
-          continue;
-        }
-        const uint32_t fin = (uint32_t)(v & 1);
-        if (rank != fin) {
-          // push this rank's partial into the finisher's receive buffer
-          if (wt == 0) swait(&S.recv_free, (pushes & 1u) ^ 1u, p.err);
-          wbar();
-          const uint32_t dst = map_rank(&S.recv[0][row][0], peer);
-          for (int c = half; c < nch; c += 2) {
-            float val[8];
-            tmem_chunk(t_base, c, val);
-            if (valid) {
-              st_cluster_v4(dst + (uint32_t)((2 * c) * 128 * 16), val[0], val[1], val[2], val[3]);
-              st_cluster_v4(dst + (uint32_t)((2 * c + 1) * 128 * 16), val[4], val[5], val[6], val[7]);
+          float sq[8];
+          finish(op, l, n, valid, c, nlive, val, sq);
+          if (op == kO) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sq[i] = warp_sum(sq[i]);
+            if (lane == 0) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (c * 8 + i < M) S.red[quad][c * 8 + i] += sq[i];
             }
           }
-          mbar_arrive_remote(map_rank(&S.recv_full, peer));
-          if (wt == 0 && uu == 0) stamp(p, cta, ph, kTrPushed);
-          ++pushes;
-        } else {
-          swait_cluster(&S.recv_full, recvs & 1u, p.err);
-          if (wt == 0 && uu == 0) stamp(p, cta, ph, kTrRecv);
-          if (op == kO) did_o_finish = true;
-          for (int c = half; c < nch; c += 2) {
-            float val[8];
-            tmem_chunk(t_base, c, val);
-            const float4 ra = *reinterpret_cast<const float4*>(&S.recv[2 * c][row][0]);
-            const float4 rb = *reinterpret_cast<const float4*>(&S.recv[2 * c + 1][row][0]);
-            val[0] += ra.x;
-            val[1] += ra.y;
-            val[2] += ra.z;
-            val[3] += ra.w;
-            val[4] += rb.x;
-            val[5] += rb.y;
-            val[6] += rb.z;
-            val[7] += rb.w;
-            float sq[8];
-            finish(op, l, n, valid, c, min(8, M - c * 8), val, sq);
-            if (op == kO) {
-              // this quadrant's share of each token's sum of squares
-#pragma unroll
-              for (int i = 0; i < 8; ++i) sq[i] = warp_sum(sq[i]);
-              if (lane == 0) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                  if (c * 8 + i < M) S.red[quad][c * 8 + i] = sq[i];
-              }
-            }
-          }
-          wbar();  // the receive buffer is consumed
-          if (wt == 0) mbar_arrive_remote(map_rank(&S.recv_free, peer));
-          ++recvs;
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.acc_empty[b]);
-      ++units;
+      if (b) ++use1; else ++use0;
     }
     if (op == kO) {
-      // this rank's slot of the o projection's sums of squares (zero if it finished nothing)
+      // this CTA's slot of the o projection's sums of squares (zero if it has no rows)
       wbar();
-      if (wt < M)
-        p.ss_o[cta * NT + wt] =
-            did_o_finish ? (S.red[2][wt] + S.red[3][wt]) + (S.red[0][wt] + S.red[1][wt]) : 0.f;
+      if (wt < M) p.ss_o[cta * NT + wt] = (S.red[2][wt] + S.red[3][wt]) + (S.red[0][wt] + S.red[1][wt]);
     }
     if (op == kHead) {
       wbar();
@@ -1007,8 +972,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     mbar_init(&S.acc_empty[1], kWorkers / 32);
     mbar_init(&S.b_full, 1);
     mbar_init(&S.b_empty, 1);
-    mbar_init(&S.recv_full, kWorkers);
-    mbar_init(&S.recv_free, 1);
     fence_barrier_init();
   }
   if (threadIdx.x == 32) S.sh.init(cta, p.vocab);
@@ -1026,9 +989,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = S.tmem_slot;
-  // the pair's barrier initialisations are visible before any remote arrival
-  cluster_arrive();
-  cluster_wait();
 
   if (warp == 0) {
     run_producer(p, S, ring, cta, lane, S.sh);
@@ -1049,9 +1009,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
   }
   tc_fence_before();
   __syncthreads();
-  // the peer may still be reading this CTA's shared memory (pair exchange)
-  cluster_arrive();
-  cluster_wait();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, p.tmem_cols);
@@ -1062,20 +1019,30 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
 
 int step_ring_slots(int NT) {
   const size_t room = 227 * 1024 - kFixedBytes - b_region_bytes(NT);
-  int s = (int)(room / kSlotBytes);
-  return s > kMaxSlots ? kMaxSlots : s;
+  int slots = (int)(room / kSlotBytes);
+  return slots > kMaxSlots ? kMaxSlots : slots;
 }
 
 size_t step_smem_bytes(int NT) {
   return kFixedBytes + (size_t)step_ring_slots(NT) * kSlotBytes + b_region_bytes(NT);
 }
 
-bool step_supported() {
-  return sm_count() == kGrid;
+int step_chains(int NT) { return NT <= 16 ? 8 : 4; }
+
+uint32_t step_tmem_cols(int NT) {
+  // two tiles of `chains` accumulators of 2 NT columns each, rounded to a power of two
+  uint32_t need = 2u * (uint32_t)step_chains(NT) * 2u * (uint32_t)NT, cols = 32;
+  while (cols < need) cols <<= 1;
+  return cols;
 }
+
+bool step_supported() { return sm_count() == kGrid; }
 
 cudaError_t launch_step(const StepParams& p, cudaStream_t stream) {
   const size_t smem = step_smem_bytes(p.NT);
+  if (p.slots != step_ring_slots(p.NT) || p.chains != step_chains(p.NT) || p.tmem_cols != step_tmem_cols(p.NT) ||
+      p.tmem_cols > 512)
+    return cudaErrorInvalidValue;
   cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(step_kernel), (int)smem);
   if (e != cudaSuccess) return e;
   e = cudaMemsetAsync(p.ctr, 0, sizeof(unsigned) * kCounterStride * (size_t)(1 + kPhasesPerLayer * p.n_layers),
@@ -1086,15 +1053,11 @@ cudaError_t launch_step(const StepParams& p, cudaStream_t stream) {
   cfg.blockDim = dim3(kStepThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: phases wait on each other
   attr[0].val.cooperative = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = 2;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, step_kernel, p);
 }
 

@@ -57,8 +57,9 @@ struct StepParams {
   unsigned long long* argmax;  // (M) packed argmax slots
   int* err;
   unsigned long long* trace;  // optional per-CTA phase timestamps (kTraceEvents per phase), or null
-  int slots;           // ring slots
-  uint32_t tmem_cols;
+  int slots;           // ring slots (step_ring_slots)
+  int chains;          // independent accumulators per tile (step_chains, a power of two)
+  uint32_t tmem_cols;  // step_tmem_cols
 };
 
 // Optional timeline of a launch (StepParams::trace): globaltimer stamps (ns) at
@@ -77,13 +78,15 @@ enum StepTraceEvent : int {
   kTrPushed = 7,    // pushing rank: its partial is pushed
 };
 
-// Shared memory of one step CTA for token tile NT, and its ring slot count.
+// Shared memory of one step CTA for token tile NT, its ring slot count, accumulator chains
+// per tile and TMEM columns.
 size_t step_smem_bytes(int NT);
 int step_ring_slots(int NT);
-// Launches the step kernel (cooperative, 148 CTAs in clusters of 2); zeroes the phase
-// counters first.
+int step_chains(int NT);
+uint32_t step_tmem_cols(int NT);
+// Launches the step kernel (cooperative, 148 CTAs); zeroes the phase counters first.
 cudaError_t launch_step(const StepParams& p, cudaStream_t stream);
-// Whether this device can run it (148 SMs, cooperative launch of clusters of 2).
+// Whether this device can run it (148 SMs).
 bool step_supported();
 
 }  // namespace qi

@@ -1,12 +1,12 @@
 // Work partition of the decode-step kernel (step.cu), shared by host and device code so
 // that the host can check it (tests/native/step_plan_check.cpp).
 //
-// The step kernel runs on 148 CTAs, one per SM, as 74 clusters of 2 ("pairs"). For each
-// projection of a layer a pair owns a contiguous range of 8-row weight groups; rank r of
-// the pair multiplies k blocks [7r, 7r + 7) of the 14 (K = 896) and the two partial
-// products are summed in one rank's shared memory. The down projection (K = 4864) is
-// split over 147 CTAs instead: m-tile i (128 rows) x k range j of 21 ranges, partial sums
-// added by the reduce phase. The head (151936 rows) is split like the layer projections.
+// The step kernel runs on 148 CTAs, one per SM. For each projection with K = 896 (QKV, o,
+// gate/up and the tied head) a CTA owns a contiguous range of 8-row weight groups and
+// multiplies them over the whole of K, so every output row is finished by the CTA that
+// computes it (no partial sums cross CTAs). The down projection (K = 4864) is split over
+// 147 CTAs instead: m-tile i (128 rows) x k range j of 21 ranges, partial sums added by
+// the reduce phase.
 //
 // Weight pieces: the part of one 128 x 64 weight block (one m-tile, one k block) that a
 // CTA multiplies is `rows / 8` contiguous 1 KB groups of the tiled layout. Pieces are
@@ -24,8 +24,7 @@ namespace qi {
 namespace step {
 
 constexpr int kGrid = 148;            // CTAs: one per SM
-constexpr int kPairs = kGrid / 2;     // clusters of 2
-constexpr int kSlotKB = 17;           // ring slot (KB): holds the pieces of one k block of a pair
+constexpr int kSlotKB = 18;           // ring slot (KB): the pieces of two k blocks of a CTA's gate/up rows
 constexpr int kMaxTokens = 32;        // tokens of one decode step
 constexpr int kDownRanges = 21;       // k ranges of the down projection
 constexpr int kDownCtas = 7 * kDownRanges;
@@ -40,9 +39,9 @@ __host__ __device__ inline int op_groups(int op, int vocab) {
 }
 __host__ __device__ inline int op_kblocks(int op) { return op == kDown ? 76 : 14; }
 
-// A CTA's share of one projection: weight groups [g0, g1) (the same for both ranks of a
-// pair), k blocks [kb0, kb1). tile_major: pieces ordered tile by tile (the head, whose
-// tiles are finished one by one), else k block by k block (one accumulation unit).
+// A CTA's share of one projection: weight groups [g0, g1), k blocks [kb0, kb1).
+// tile_major: pieces ordered tile by tile (the head, whose tiles are finished one by one),
+// else k block by k block (one accumulation unit).
 struct Part {
   int g0, g1, kb0, kb1;
   bool tile_major;
@@ -76,16 +75,16 @@ __host__ __device__ inline Part part_of(int op, int cta, int vocab) {
     return P;
   }
   const long long G = op_groups(op, vocab);
-  const int pr = cta >> 1, r = cta & 1;
-  P.g0 = (int)(G * pr / kPairs);
-  P.g1 = (int)(G * (pr + 1) / kPairs);
-  P.kb0 = 7 * r;
-  P.kb1 = 7 * r + 7;
+  P.g0 = (int)(G * cta / kGrid);
+  P.g1 = (int)(G * (cta + 1) / kGrid);
+  P.kb0 = 0;
+  P.kb1 = 14;
   return P;
 }
 
 // Accumulation units of a share: the head has one per tile (finished one by one); the
 // layer projections one for all their tiles (at most 2).
+constexpr int kMaxLayerTiles = 2;
 __host__ __device__ inline int units_of(const Part& P) { return P.empty() ? 0 : (P.tile_major ? P.ntiles() : 1); }
 
 // One weight piece: tile u (relative), k block kb, groups [lo, hi) of the tile's 16.

@@ -39,6 +39,24 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_taddr, uint64_t adesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
       : "memory");
 }
+// The four UMMAs (K = 16 each) of one 64-column k block: A and B descriptors of the block's
+// first core-matrix column, stepped by 256 bytes (16 in the descriptors' address field,
+// which cannot carry: shared addresses stay below 256 KB). `acc0` is the accumulate flag of
+// the first UMMA; the other three always accumulate.
+__device__ __forceinline__ void umma_bf16_kblock(uint32_t d_taddr, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, %4, %4;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %5, %6, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %7, %8, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %9, %10, %3, q;\n\t}" ::"r"(d_taddr),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc0), "l"(adesc + 16), "l"(bdesc + 16), "l"(adesc + 32),
+      "l"(bdesc + 32), "l"(adesc + 48), "l"(bdesc + 48)
+      : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");

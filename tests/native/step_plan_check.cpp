@@ -1,8 +1,8 @@
 // Checks the decode-step kernel's work partition (qweninfer_b200/csrc/step_plan.h) on the
 // host: every (8-row group, k block) cell of every projection is multiplied by exactly
 // one CTA, no ring slot holds more than kSlotKB KB of pieces, no piece straddles a tile,
-// layer projections give a CTA at most two tiles (the TMEM budget) and the head one tile
-// per accumulation unit; the attention and reduce units are each owned by one CTA.
+// layer projections give a CTA at most two tiles (the TMEM budget), K = 896 shares span
+// the whole of K and the head has one tile per accumulation unit; the attention and reduce units are each owned by one CTA.
 // Prints "ok" or the first violation (exit code 1).
 #include <cstdio>
 #include <vector>
@@ -25,9 +25,8 @@ int main() {
       const Part P = part_of(op, cta, vocab);
       if (P.empty()) continue;
       if (P.g0 < 0 || P.g1 > G || P.kb0 < 0 || P.kb1 > KB) return fail("share out of range", op, cta);
-      if (op != kHead && P.ntiles() > 2) return fail("more than two tiles", op, cta);
-      if (op != kDown && (cta & 1) && (part_of(op, cta - 1, vocab).g0 != P.g0 || part_of(op, cta - 1, vocab).g1 != P.g1))
-        return fail("pair ranks own different rows", op, cta);
+      if (op != kHead && P.ntiles() > kMaxLayerTiles) return fail("more than two tiles", op, cta);
+      if (op != kDown && (P.kb0 != 0 || P.kb1 != KB)) return fail("a K = 896 share is not the whole of K", op, cta);
       std::vector<int> slot_kb(4096, 0);
       int units_first = 0, units_last = 0, last_slot = -1;
       const int n = for_each_piece(P, 0, [&](const Piece& pc, int slot, int off, bool first, bool last) {
