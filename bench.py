@@ -72,7 +72,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-window-steps", type=int, default=10,
                     help="engine steps of the window the in-process cpu_baseline times")
-    ap.add_argument("--only", choices=["decode", "batch1", "prefill", "serve64"], default=None,
+    ap.add_argument("--only", choices=["decode", "batch1", "prefill", "serve64", "serve3072"], default=None,
                     help="one measurement alone (profiling cases): graph-replayed decode steps at --batch, "
                          "config-1 batch-1 decode, config-2 prefill, config-3 64 padded slots")
     ap.add_argument("--batch", type=int, default=22, help="decode batch of --only decode")
@@ -164,6 +164,7 @@ class TimedRunner:
         self.prefill_ms = self.decode_ms = 0.0
         self.decode_bytes = 0
         self.decode_rows: list[int] = []
+        self.decode_inputs: list[tuple] = []
         self.prefill_tokens = 0
 
     def _timed(self, fn, *a):
@@ -193,6 +194,7 @@ class TimedRunner:
             self.decode_ms += ms
             self.decode_bytes += step_bytes(list(pos))
             self.decode_rows.append(len(toks))
+            self.decode_inputs.append((list(toks), list(pos), row_start))
         return out
 
 
@@ -230,7 +232,9 @@ def run_trace(eng, timed: TimedRunner, workload, window=WINDOW) -> dict:
                              "prefill_tokens": timed.prefill_tokens,
                              "mean_batch": float(np.mean(timed.decode_rows)) if timed.decode_rows else 0.0,
                              "launches": eng.runner.launches - l0, "h2d": eng.runner.h2d_bytes - hb0,
-                             "d2h": eng.runner.d2h_bytes - db0}
+                             "d2h": eng.runner.d2h_bytes - db0,
+                             "mid_decode": timed.decode_inputs[len(timed.decode_inputs) // 2]
+                             if timed.decode_inputs else None}
             full_dev += timed.prefill_ms + timed.decode_ms
             timed.reset()
     ev[1].record()
@@ -246,42 +250,9 @@ def run_trace(eng, timed: TimedRunner, workload, window=WINDOW) -> dict:
     return out
 
 
-def our_arm(args, rank: int, world: int, device: torch.device) -> dict | None:
-    from qweninfer_b200 import synthetic
-    from qweninfer_b200.engine.engine import Engine
-
-    model = load_model(device)
-    workload = synthetic.serving96()
-    eng = Engine(model, max_slots=args.slots, max_len=MAX_LEN)
-    timed = TimedRunner(eng.runner)
-    timed.active = True
-    for _ in range(args.warmup):
-        run_trace(eng, timed, workload)
-    eng.runner.check()
-
-    clocks = ClockSampler(device.index or 0)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    clocks.start()
-    runs = [run_trace(eng, timed, workload) for _ in range(args.steps)]
-    torch.cuda.synchronize()
-    clock_info = clocks.stop()
-    eng.runner.check()
-    W = {k: sum(r["window"][k] for r in runs) for k in runs[0]["window"]}
-    F = {k: sum(r["full"][k] for r in runs) for k in ("tokens", "dev_ms", "e2e_ms", "launches", "h2d", "d2h")}
-    dev_ms, e2e_ms, tokens = W["dev_ms"], W["e2e_ms"], float(W["tokens"])
-    if world > 1:
-        t = torch.tensor([dev_ms, e2e_ms, tokens], device=device, dtype=torch.float64)
-        mx, sm = t.clone(), t.clone()
-        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
-        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
-        dev_ms, e2e_ms, tokens = float(mx[0]), float(mx[1]), float(sm[2])
-        torch.distributed.barrier()
-    if rank != 0:
-        return None
+def main_line(args, world, eng, runs, W, F, dev_ms, e2e_ms, tokens, clock_info, pk) -> dict:
+    """Rank 0's JSON line of the serving window."""
     K = args.steps
-    pk = peaks()
     launch_s = W["decode_ms"] / 1e3 / max(1, W["decode_steps"])
     algo = W["decode_bytes"] / max(1, W["decode_steps"])
     gbs = algo / launch_s / 1e9
@@ -310,13 +281,12 @@ def our_arm(args, rank: int, world: int, device: torch.device) -> dict | None:
         "window": {"output_tokens_per_step": W["tokens"] // K, "decode_steps_per_step": W["decode_steps"] // K,
                    "mean_decode_batch": W["mean_batch"] / K, "decode_ms_per_decode_step": launch_s * 1e3,
                    "prefill_ms_per_step": W["prefill_ms"] / K, "prefill_tokens_per_step": W["prefill_tokens"] // K},
-        "roofline": {"kernel": "step_kernel: the whole decode-step forward in one cooperative launch (embedding, "
-                               "24 layers, head + argmax), over the window's decode steps", "bound": "hbm",
-                     "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"],
-                     "peak_source": pk["source"], "traffic": None,
-                     "algorithmic_bytes_per_launch": algo, "us_per_launch": launch_s * 1e6,
-                     "bytes": "988,065,536 weights + sum(len+1)*12,288 KV read + B*12,288 KV write + B*1,792 "
-                              "embed, per decode step"},
+        "step_roofline": {"what": "the whole decode step (embedding, 24 layers, head + argmax; one CUDA graph "
+                                  "of the launches below), over the window's decode steps", "bound": "hbm",
+                          "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"],
+                          "algorithmic_bytes_per_step": algo, "us_per_step": launch_s * 1e6,
+                          "bytes": "988,065,536 weights + sum(len+1)*12,288 KV read + B*12,288 KV write + "
+                                   "B*1,792 embed, per decode step"},
         "full_trace": {"value": F["tokens"] / (F["dev_ms"] / 1e3), "e2e": F["tokens"] / (F["e2e_ms"] / 1e3),
                        "unit": "tok/s", "output_tokens": F["tokens"] // K, "engine_steps": runs[0]["full"]["steps"],
                        "ttft_mean_s": statistics.mean(r["full"]["ttft_mean_s"] for r in runs),
@@ -324,11 +294,104 @@ def our_arm(args, rank: int, world: int, device: torch.device) -> dict | None:
                        "gpu_launches_per_trace": F["launches"] // K},
         "clocks": clock_info,
     }
+    mid = runs[-1]["window"]["mid_decode"]
+    if mid is not None:
+        kt = kernel_table(eng.runner, mid, pk)
+        top = max(kt["kernels"].values(), key=lambda e: e["share"])
+        res["roofline"] = {"kernel": top["kernel"], "bound": "hbm", "achieved": top["achieved_gbs"],
+                           "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": top["frac"], "peak_source": pk["source"],
+                           "traffic": None, "algorithmic_bytes_per_launch": top["algorithmic_bytes_per_launch"],
+                           "us_per_launch": top["us_per_launch"], "share": top["share"],
+                           "measured_at": f"decode batch {kt['batch']}, mean position {kt['mean_position']:.0f} "
+                                          "(the window's middle decode step), each launch timed alone"}
+        res["kernels"] = kt
+    return res
+
+
+def our_arm(args, rank: int, world: int, device: torch.device) -> dict | None:
+    from qweninfer_b200 import synthetic
+    from qweninfer_b200.engine.engine import Engine
+
+    model = load_model(device)
+    workload = synthetic.serving96()
+    eng = Engine(model, max_slots=args.slots, max_len=MAX_LEN)
+    timed = TimedRunner(eng.runner)
+    timed.active = True
+    for _ in range(args.warmup):
+        run_trace(eng, timed, workload)
+    eng.runner.check()
+
+    clocks = ClockSampler(device.index or 0)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    runs = [run_trace(eng, timed, workload) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    eng.runner.check()
+    W = {k: sum(r["window"][k] for r in runs) for k in runs[0]["window"] if k != "mid_decode"}
+    F = {k: sum(r["full"][k] for r in runs) for k in ("tokens", "dev_ms", "e2e_ms", "launches", "h2d", "d2h")}
+    dev_ms, e2e_ms, tokens = W["dev_ms"], W["e2e_ms"], float(W["tokens"])
+    if world > 1:
+        t = torch.tensor([dev_ms, e2e_ms, tokens], device=device, dtype=torch.float64)
+        mx, sm = t.clone(), t.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
+        dev_ms, e2e_ms, tokens = float(mx[0]), float(mx[1]), float(sm[2])
+        torch.distributed.barrier()
+    pk = peaks()
+    res = main_line(args, world, eng, runs, W, F, dev_ms, e2e_ms, tokens, clock_info, pk) if rank == 0 else None
+    if not args.no_extras:
+        s4 = serve3072(model, rank, world, device, pk)
+        if res is not None:
+            res["serve3072"] = s4
     if world == 1 and not args.no_extras:
         res["batch1"] = batch1_latency(model, pk)
         res["prefill"] = prefill_ttft(model, pk)
         res["serve64_padded"] = serve64(model)
     return res
+
+
+# Algorithmic HBM bytes of one launch of each kind at decode batch B (positions pos): the
+# weights it must stream, the KV bytes it must read or append, the embedding rows. The
+# activations between launches stay in L2 and are not counted.
+KERNEL_NAMES = {"embed": "embed_kernel", "qkv": "tc_proj_kernel<qkv_rope>", "attention": "attention_kernel",
+                "o_proj": "tc_proj_kernel<residual> (o_proj)", "gate_up": "tc_proj_kernel<swiglu>",
+                "down": "tc_proj_kernel<residual> (down)", "head": "tc_proj_kernel<logits>"}
+
+
+def kernel_bytes(pos: list[int]) -> dict:
+    B = len(pos)
+    kv_row = 2 * 2 * 64 * 2  # K and V, 2 KV heads x 64 dims, bf16: per cached token and layer
+    return {"embed": B * EMBED_ROW_BYTES, "qkv": 1152 * 896 * 2 + 1152 * 4 + B * kv_row,
+            "attention": sum(p + 1 for p in pos) * kv_row, "o_proj": 896 * 896 * 2,
+            "gate_up": 9728 * 896 * 2, "down": 896 * 4864 * 2, "head": 151936 * 896 * 2}
+
+
+def kernel_table(runner, decode_input, pk: dict, reps: int = 5) -> dict:
+    """Every launch of one decode step timed alone with CUDA events (`launch_times`), at a
+    decode step of the timed window (its batch and positions): per kind launches per step,
+    microseconds per launch, algorithmic bytes, achieved GB/s and fraction of the measured
+    copy peak, and share of the step's summed launch time."""
+    toks, pos, row_start = decode_input
+    runner.launch_times(toks, pos, row_start)
+    acc: dict[str, list[float]] = {}
+    for _ in range(reps):
+        for k, us in runner.launch_times(toks, pos, row_start):
+            acc.setdefault(k, []).append(us)
+    runner.check()
+    algo = kernel_bytes(pos)
+    total = sum(sum(v) for v in acc.values())
+    table = {}
+    for k, v in acc.items():
+        mean = sum(v) / len(v)
+        gbs = algo[k] / (mean * 1e-6) / 1e9
+        table[k] = {"kernel": KERNEL_NAMES[k], "launches_per_step": len(v) // reps, "us_per_launch": mean,
+                    "algorithmic_bytes_per_launch": algo[k], "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"],
+                    "share": sum(v) / total}
+    return {"batch": len(toks), "mean_position": float(np.mean(pos)), "sum_us_per_step": total / reps,
+            "kernels": table}
 
 
 def decode_steps(model, B: int, steps: int, warmup: int) -> dict:
@@ -429,6 +492,73 @@ def serve64(model) -> dict:
             "pad_sizes": sorted(set(pad_to[1:])), "autotune_ms": {str(k): v for k, v in ms.items()}}
 
 
+def serve3072(model, rank: int, world: int, device: torch.device, pk: dict) -> dict | None:
+    """Config 4: the scaled serving trace (3072 requests at t=0, prompts U[128,2048],
+    outputs lognormal(200,0.9) <= 1024, seed 5) over `world` replicas, one per GPU, each
+    with 128 slots and max_len 4096, dispatched rid % world through ReplicaGroup (results
+    published to the process group's store). Whole-box tok/s = all output tokens / the
+    slowest rank's time (CUDA events around its serve, host scheduling included; the
+    device-only figure sums each rank's forward times). Per-GPU HBM fraction: algorithmic
+    bytes of the decode steps / their device time, over all ranks. Total work is fixed, so
+    this is strong scaling."""
+    from qweninfer_b200 import synthetic
+    from qweninfer_b200.engine.engine import Engine, Request
+    from qweninfer_b200.engine.replicas import ReplicaGroup
+    slots, max_len = 128, 4096
+    reqs = [Request(r.rid, r.prompt, r.max_new_tokens)
+            for r in synthetic.serving_requests(3072, 128, 2048, 200.0, 0.9, 1024, seed=5)]
+    eng = Engine(model, max_slots=slots, max_len=max_len)
+    # warm-up outside the timed region: every decode batch size's graph, the prefill workspace
+    for B in range(1, slots + 1):
+        eng.runner.decode([0] * B, [0] * B)
+    eng.runner.prefill_many([0, 1], [[0] * 2048, [0] * 2048])
+    timed = TimedRunner(eng.runner)
+    timed.active = True
+    if world > 1:
+        store = torch.distributed.distributed_c10d._get_default_store()
+    else:
+        store = torch.distributed.HashStore()
+    group = ReplicaGroup(lambda: eng, rank, world, store, prefix="serve3072", timeout_s=300.0)
+    mine = [r for r in reqs if r.rid % world == rank]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev[0].record()
+    group.serve(reqs, collect=False)
+    ev[1].record()
+    ev[1].synchronize()
+    eng.runner.check()
+    wall_ms = ev[0].elapsed_time(ev[1])
+    done = group.results(mine)
+    t = torch.tensor([wall_ms, timed.prefill_ms + timed.decode_ms, sum(len(r.output) for r in done),
+                      timed.decode_bytes, timed.decode_ms, timed.prefill_ms, timed.prefill_tokens,
+                      len(timed.decode_rows), sum(timed.decode_rows),
+                      statistics.mean(r.first_token - r.arrival for r in done) if done else 0.0],
+                     dtype=torch.float64, device=device)
+    if world > 1:
+        mx, sm = t.clone(), t.clone()
+        torch.distributed.all_reduce(mx, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(sm, op=torch.distributed.ReduceOp.SUM)
+        torch.distributed.barrier()
+    else:
+        mx = sm = t
+    if rank != 0:
+        return None
+    tokens = float(sm[2])
+    gbs = float(sm[3]) / (float(sm[4]) / 1e3) / 1e9 / world
+    return {"workload": "serve3072: 3072 requests (prompts U[128,2048], outputs lognormal(200,0.9)<=1024, seed 5), "
+                        f"rid % {world} over {world} replica(s), {slots} slots and max_len {max_len} per GPU",
+            "value": tokens / (float(mx[0]) / 1e3), "unit": "tok/s", "scaling": "strong",
+            "device_value": tokens / (float(mx[1]) / 1e3), "output_tokens": int(tokens),
+            "max_rank_ms": float(mx[0]), "max_rank_device_ms": float(mx[1]),
+            "decode_hbm_gbs_per_gpu": gbs, "decode_frac_per_gpu": gbs / pk["hbm_gbs"],
+            "decode_ms_total": float(sm[4]), "prefill_ms_total": float(sm[5]),
+            "prefill_tokens": int(sm[6]), "decode_steps": int(sm[7]),
+            "mean_decode_batch": float(sm[8]) / max(1.0, float(sm[7])),
+            "ttft_mean_s": float(sm[9]) / world}
+
+
 # ------------------------------------------------------------- CPU arms
 
 def cpu_threads() -> int:
@@ -523,6 +653,17 @@ def main() -> None:
         return
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.only == "serve3072":  # every rank serves its share
+        if world > 1:
+            torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+        try:
+            r = serve3072(load_model(device), rank, world, device, peaks())
+            if rank == 0:
+                print(json.dumps(r), flush=True)
+        finally:
+            if world > 1:
+                torch.distributed.destroy_process_group()
+        return
     if args.only is not None:
         model = load_model(device)
         pk = peaks()

@@ -243,6 +243,29 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
                int head_stride, int n_head, void* logits, int logits_bf16, long long logits_ld,
                unsigned long long* argmax_slots, qi_stream_t stream);
 
+/* Launch kinds reported by qi_forward_launch_times. */
+#define QI_LAUNCH_EMBED 0     /* embedding gather + first activation tiles      */
+#define QI_LAUNCH_QKV 1       /* RMSNorm + QKV + bias + RoPE + KV append         */
+#define QI_LAUNCH_ATTENTION 2 /* ragged GQA attention core                       */
+#define QI_LAUNCH_O 3         /* o_proj + residual                               */
+#define QI_LAUNCH_GATE_UP 4   /* RMSNorm + gate/up + SwiGLU                      */
+#define QI_LAUNCH_DOWN 5      /* down + residual                                 */
+#define QI_LAUNCH_HEAD 6      /* final RMSNorm + tied head + argmax              */
+
+/* qi_forward (tensor-core projections, ws->use_tc != 0) with a CUDA event recorded before
+ * the first launch and after every launch: kinds[i] (QI_LAUNCH_*) and us[i] (microseconds
+ * of device time) of launch i, *n_launches launches (<= max_launches, else
+ * QI_ERR_TOO_LARGE). The events serialize the launches, so each time is that launch alone,
+ * without the overlap that programmatic dependent launch gives the plain forward.
+ * Synchronizes the stream. Instrumentation for per-kernel rooflines; no reference
+ * counterpart (the reference's forward is qweninfer/models/qwen2.py:263-292). */
+int qi_forward_launch_times(const qi_model* model, const qi_cache* cache, const qi_workspace* ws,
+                            const int32_t* ids, const int32_t* pos, const int32_t* rows, int M,
+                            int head_lo, int head_stride, int n_head, void* logits, int logits_bf16,
+                            long long logits_ld, unsigned long long* argmax_slots,
+                            qi_stream_t stream, int* kinds, float* us, int max_launches,
+                            int* n_launches);
+
 /* ---------------------------------------------------------- decode step */
 
 /* One batched decode step of M <= 32 rows as ONE cooperative launch (148 CTAs, one per

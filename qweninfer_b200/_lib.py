@@ -21,6 +21,8 @@ QI_ERR_TIMEOUT = 1002
 QI_ERR_DEVICE = 1003
 QI_ERR_TOO_LARGE = 1004
 QI_ERR_INDEX = 1005
+# launch kinds of qi_forward_launch_times
+LAUNCH_KINDS = ("embed", "qkv", "attention", "o_proj", "gate_up", "down", "head")
 
 vp = C.c_void_p
 i32 = C.c_int
@@ -72,6 +74,8 @@ SIGNATURES = {
                          i32, i32, i32, i32, vp, i32, i64, vp, vp]),
     "qi_decode_step": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp, i32, vp,
                              i32, i64, vp, vp]),
+    "qi_forward_launch_times": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp,
+                                      i32, i32, i32, i32, vp, i32, i64, vp, vp, vp, vp, i32, vp]),
     "qi_act_tiles": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp]),
     "qi_tc_linear": (i32, [vp, i32, i32, vp, i32, i32, vp, i32, f32, vp, i32, vp, i64, vp, i32, i32, vp, vp]),
     "qi_tc_gate_up_swiglu": (i32, [vp, vp, i32, i32, vp, i32, f32, vp, vp, i64, vp, i32, i32, vp, vp]),

@@ -350,9 +350,30 @@ int grid_for(int n_tiles, int KB, int max_contrib) {
 // qi_forward on the tensor-core path: every projection is a tc_proj launch whose
 // epilogue writes the next projection's activation tiles (the RMSNorm weights folded in,
 // the per-token RMS applied in the consumer's epilogue from partial sums of squares).
+// Per-launch device times of one forward: an event recorded before the first launch and
+// after every launch (qi_forward_launch_times). The events separate the launches, so each
+// time is the launch's own duration without the programmatic-dependent-launch overlap.
+struct LaunchTimer {
+  cudaStream_t s;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> kind;
+  int mark(int k) {
+    cudaEvent_t e;
+    const int r = rc(cudaEventCreate(&e));
+    if (r != QI_OK) return r;
+    ev.push_back(e);
+    kind.push_back(k);
+    return rc(cudaEventRecord(e, s));
+  }
+  ~LaunchTimer() {
+    for (cudaEvent_t e : ev) cudaEventDestroy(e);
+  }
+};
+
 int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
                const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
-               void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots, cudaStream_t s) {
+               void* logits, int logits_bf16, long long logits_ld, unsigned long long* slots, cudaStream_t s,
+               LaunchTimer* lt = nullptr) {
   int tiles[5];
   token_tiles(M, tiles);
   // a workspace padded less than to 128 tokens gets the largest tiles that fit it
@@ -371,9 +392,12 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
   if (!ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss || !ws->tc_scratch || !ws->tc_counters)
     return QI_ERR_ARG;
   const bool pdl = true;
-  int r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, slots, n_head, s, false, model->layers[0].ln1, NT,
-                          ws->act_x, ws->ss, ws->ss_ld));
+  auto mark = [&](int kind) { return lt ? lt->mark(kind) : QI_OK; };
+  int r = mark(-1);
   if (r != QI_OK) return r;
+  r = rc(launch_embed(model->embed, model->vocab, ids, M, ws->x, slots, n_head, s, false, model->layers[0].ln1, NT,
+                      ws->act_x, ws->ss, ws->ss_ld));
+  if (r != QI_OK || (r = mark(QI_LAUNCH_EMBED)) != QI_OK) return r;
   TcParams base = {};
   base.M = M;
   base.ss_ld = ws->ss_ld;
@@ -404,7 +428,9 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     int caps[5];
     tc_caps(caps, p.NT);
     const int g = grid_for(p.n_mtiles * p.n_ntiles, p.KB, caps[j]);
-    return run_tc(p, ws->tc_scratch, ws->tc_scratch_floats, ws->tc_counters, ws->tc_counters_len, g, s, pdl);
+    const int kinds[5] = {QI_LAUNCH_QKV, QI_LAUNCH_O, QI_LAUNCH_GATE_UP, QI_LAUNCH_DOWN, QI_LAUNCH_HEAD};
+    const int r = run_tc(p, ws->tc_scratch, ws->tc_scratch_floats, ws->tc_counters, ws->tc_counters_len, g, s, pdl);
+    return r != QI_OK ? r : mark(kinds[j]);
   };
   const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
   for (int li = 0; li < model->num_layers; ++li) {
@@ -432,7 +458,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     if ((r = launch(p, 0)) != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
                   ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, tiles[1], cache->cache_rows);
-    if (r != QI_OK) return r;
+    if (r != QI_OK || (r = mark(QI_LAUNCH_ATTENTION)) != QI_OK) return r;
     p = params(1, tiles[2]);  // o_proj + residual; emits RMSNorm(post_attention) inputs
     p.w = L.w_o;
     p.KB = kHidden / 64;
@@ -490,6 +516,18 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     }
   }
   return QI_OK;
+}
+
+bool bad_forward_args(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
+                      const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
+                      const void* logits, long long logits_ld, const unsigned long long* argmax_slots) {
+  return !model || !cache || !ws || !model->layers || M <= 0 || M > ws->max_tokens || n_head < 0 ||
+         (n_head > 0 &&
+          (head_lo < 0 || head_stride < 1 || (long long)head_lo + (long long)(n_head - 1) * head_stride >= M)) ||
+         bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || (n_head > 0 && bad_ptr(argmax_slots)) ||
+         (logits && logits_ld < model->vocab) || model->vocab % kTileRows != 0 || model->num_layers <= 0 ||
+         ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len ||
+         ws->max_splits > kMaxAttnSplits || cache->max_len > model->max_seq;
 }
 
 }  // namespace
@@ -726,12 +764,8 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
                const int32_t* pos, const int32_t* rows, int M, int head_lo, int head_stride, int n_head,
                void* logits, int logits_bf16, long long logits_ld, unsigned long long* argmax_slots,
                qi_stream_t stream) {
-  if (!model || !cache || !ws || !model->layers || M <= 0 || M > ws->max_tokens || n_head < 0 ||
-      (n_head > 0 && (head_lo < 0 || head_stride < 1 || (long long)head_lo + (long long)(n_head - 1) * head_stride >= M)) ||
-      bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || (n_head > 0 && bad_ptr(argmax_slots)) ||
-      (logits && logits_ld < model->vocab) || model->vocab % kTileRows != 0 || model->num_layers <= 0 ||
-      ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len ||
-      ws->max_splits > kMaxAttnSplits || cache->max_len > model->max_seq)
+  if (bad_forward_args(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits, logits_ld,
+                       argmax_slots))
     return QI_ERR_ARG;
   if (ws->use_tc) return forward_tc(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits,
                                     logits_bf16, logits_ld, argmax_slots, as_stream(stream));
@@ -762,6 +796,32 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
                 model->eps, model->embed, model->vocab, n_head, logits, logits_bf16, logits_ld, argmax_slots,
                 ws->err, s, pdl);
   return r;
+}
+
+int qi_forward_launch_times(const qi_model* model, const qi_cache* cache, const qi_workspace* ws,
+                            const int32_t* ids, const int32_t* pos, const int32_t* rows, int M, int head_lo,
+                            int head_stride, int n_head, void* logits, int logits_bf16, long long logits_ld,
+                            unsigned long long* argmax_slots, qi_stream_t stream, int* kinds, float* us,
+                            int max_launches, int* n_launches) {
+  if (bad_forward_args(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits, logits_ld,
+                       argmax_slots) ||
+      !ws->use_tc || !kinds || !us || !n_launches || max_launches <= 0)
+    return QI_ERR_ARG;
+  LaunchTimer lt;
+  lt.s = as_stream(stream);
+  int r = forward_tc(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits, logits_bf16,
+                     logits_ld, argmax_slots, lt.s, &lt);
+  if (r != QI_OK) return r;
+  if ((r = rc(cudaStreamSynchronize(lt.s))) != QI_OK) return r;
+  const int n = (int)lt.ev.size() - 1;
+  if (n > max_launches) return QI_ERR_TOO_LARGE;
+  for (int i = 0; i < n; ++i) {
+    kinds[i] = lt.kind[i + 1];
+    if ((r = rc(cudaEventElapsedTime(&us[i], lt.ev[i], lt.ev[i + 1]))) != QI_OK) return r;
+    us[i] *= 1000.f;
+  }
+  *n_launches = n;
+  return QI_OK;
 }
 
 }  // extern "C"

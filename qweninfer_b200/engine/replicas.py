@@ -90,7 +90,8 @@ class ReplicaGroup:
 
     def _publish(self, req: Request) -> None:
         self.store.set(self._k("res", req.rid), json.dumps(
-            {"rid": req.rid, "output": req.output, "first_token": req.first_token, "finished": req.finished}))
+            {"rid": req.rid, "output": req.output, "arrival": req.arrival, "first_token": req.first_token,
+             "finished": req.finished}))
 
     # ------------------------------------------------------------ serving
     def _serve(self, reqs: list[Request]) -> None:
@@ -127,9 +128,10 @@ class ReplicaGroup:
             time.sleep(self.poll_s)
         return [r for r in live if self._status(rnd, r) == "failed"]
 
-    def serve(self, requests: list[Request]) -> list[Request]:
+    def serve(self, requests: list[Request], collect: bool = True) -> list[Request] | None:
         """Serve this rank's share and, with the other survivors, the share of any rank
-        that fails; returns all requests with outputs, in rid order."""
+        that fails; returns all requests with outputs, in rid order (None with
+        collect=False: the outputs stay in the store, `results` reads them)."""
         live = list(range(self.world))
         assign = {r: shard(requests, r, self.world) for r in live}
         if self.engine is None:  # before the first heartbeat: building it may take a while
@@ -153,7 +155,7 @@ class ReplicaGroup:
             assign = {r: [q for q in left if live[q.rid % len(live)] == r] for r in live}
             self.log.append(f"round {self.round}: ranks {failed} failed, {len(left)} requests reassigned")
             self.round += 1
-        return self.results(requests)
+        return self.results(requests) if collect else None
 
     def results(self, requests: list[Request]) -> list[Request]:
         """Every request of `requests` with the output published for it."""
@@ -162,5 +164,6 @@ class ReplicaGroup:
             d = json.loads(self.store.get(self._k("res", r.rid)).decode())
             q = Request(r.rid, list(r.prompt), r.max_new_tokens)
             q.output, q.first_token, q.finished = d["output"], d["first_token"], d["finished"]
+            q.arrival = d.get("arrival", q.arrival)
             out.append(q)
         return out

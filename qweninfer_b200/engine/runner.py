@@ -185,6 +185,29 @@ class DecodeRunner:
         self.steps += 1
         return self._read(B)
 
+    @torch.inference_mode()
+    def launch_times(self, toks: list[int], pos: list[int], row_start: int = 0) -> list[tuple[str, float]]:
+        """The decode step's launches, each timed alone (`qi_forward_launch_times`: an event
+        after every launch), as (kind, microseconds); writes the step's K/V like `decode`."""
+        B = len(toks)
+        if B == 0 or B > self.max_batch or row_start < 0 or row_start + B > self.cache.max_batch:
+            raise ValueError("decode batch outside the runner's rows")
+        if max(pos) >= self.cache.max_len or min(pos) < 0:
+            raise IndexError(f"position outside 0..{self.cache.max_len - 1}")
+        self._check_ids(toks)
+        self.dec.put(toks, pos, np.arange(row_start, row_start + B))
+        self.ws.plan(B)
+        cap = 8 * (2 + 5 * self.model.cfg.num_hidden_layers)
+        kinds = (C.c_int * cap)()
+        us = (C.c_float * cap)()
+        n = C.c_int(0)
+        _lib.check(_lib.lib().qi_forward_launch_times(
+            C.byref(self.model.native()), C.byref(self.cache.native()), C.byref(self.ws.struct),
+            self.dec.ptr(0), self.dec.ptr(1), self.dec.ptr(2), B, 0, 1, B, None, 0, 0,
+            self.d_slots.data_ptr(), _lib.stream_ptr(self.dev), kinds, us, cap, C.byref(n)),
+            "qi_forward_launch_times")
+        return [(_lib.LAUNCH_KINDS[kinds[i]], float(us[i])) for i in range(n.value)]
+
     def check(self) -> None:
         """Raise if a kernel recorded a timed-out wait (synchronises)."""
         self.ws.check()

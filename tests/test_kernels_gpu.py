@@ -182,6 +182,11 @@ def test_qkv_rope_append(M):
     (3, 512, [5, 127, 128]),
     (5, 1024, [0, 129, 255, 256, 1000]),
     (70, 700, None),
+    # the scaled serving cache (max_len 4096): <= 64 queries use 16 splits of 256 keys merged
+    # through global scratch, 128 queries 4 splits of 1024 keys merged in a cluster
+    (2, 4096, [4095, 2047]),
+    (64, 4096, None),
+    (128, 4096, None),
 ])
 def test_attention_ragged(M, max_len, positions):
     from qweninfer_b200.models.qwen2 import _AttnScratch

@@ -265,6 +265,28 @@ def test_decode_step_writes_only_its_slots(gpu_model):
     assert bool((slots[M:] == sentinel).all())
 
 
+def test_launch_times_match_the_forward(gpu_model):
+    """qi_forward_launch_times runs the same launches as a decode step: embed, 24 x (qkv,
+    attention, o, gate/up, down), head, each with a positive time; its greedy tokens equal
+    the graph-replayed decode step's on the same cache contents."""
+    from qweninfer_b200.engine.runner import DecodeRunner
+    B = 6
+    cache = KVCache(gpu_model.cfg, B, 64, dtype=torch.bfloat16, device="cuda")
+    r = DecodeRunner(gpu_model, cache, max_batch=B)
+    toks, pos = [5, 9, 11, 13, 17, 19], [0, 3, 7, 1, 2, 9]
+    k0, v0 = cache.k.clone(), cache.v.clone()
+    want = r.decode(toks, pos)
+    cache.k.copy_(k0)
+    cache.v.copy_(v0)
+    got = r.launch_times(toks, pos)
+    L = gpu_model.cfg.num_hidden_layers
+    kinds = ["embed"] + ["qkv", "attention", "o_proj", "gate_up", "down"] * L + ["head"]
+    assert [k for k, _ in got] == kinds
+    assert all(us > 0 for _, us in got)
+    assert np.array_equal(r._read(B), want)
+    r.check()
+
+
 def test_prefill_many_matches_single_prefills(gpu_model):
     """Several prompts in one forward (last tokens moved to the end) give the same greedy
     tokens and the same cache rows as one B = 1 prefill each; the k-split of the
