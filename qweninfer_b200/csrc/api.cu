@@ -81,6 +81,15 @@ int qkv(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv, con
 
 bool use_tc_clusters();
 
+// QI_BLOCK_ATTN=0 keeps the per-token attention kernel for prefill too (comparisons)
+bool use_block_attention() {
+  static const bool on = [] {
+    const char* v = getenv("QI_BLOCK_ATTN");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int32_t* pos, const int32_t* rows,
               int M, int max_len, int split_keys, int max_splits, float* out, float* part, unsigned int* counters,
               int* err, cudaStream_t s, bool pdl, uint16_t* out_act = nullptr, int out_nt = 0,
@@ -103,6 +112,9 @@ int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int3
   a.part = part;
   a.counters = counters;
   a.err = err;
+  // prefill-sized query counts: blocks of 16 tokens share K/V tiles (a prompt's tokens
+  // are consecutive in the forward)
+  if (M > kBlockAttnMinTokens && use_block_attention()) return rc(launch_attention_block(a, s, pdl));
   // splits of a token merged inside a cluster when a launch has 2..8 of them
   a.cluster = (use_tc_clusters() && max_splits >= 2 && max_splits <= 8) ? 1 : 0;
   return rc(launch_attention(a, s, pdl));

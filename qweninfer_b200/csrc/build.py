@@ -21,7 +21,7 @@ CSRC = Path(__file__).resolve().parent
 PKG = CSRC.parent
 REPO = PKG.parent
 LIB = PKG / "libqi.so"
-SOURCES = ["gemv.cu", "attention.cu", "misc.cu", "norm_rope.cu", "tc_proj.cu", "step.cu", "api.cu"]
+SOURCES = ["gemv.cu", "attention.cu", "attention_block.cu", "misc.cu", "norm_rope.cu", "tc_proj.cu", "step.cu", "api.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -42,7 +42,8 @@ def flags(verbose: bool) -> list[str]:
 def build(verbose: bool = False, force: bool = False) -> Path:
     objdir = PKG / "_build"
     objdir.mkdir(exist_ok=True)
-    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [REPO / "include" / "qi.h"]
+    deps = [CSRC / s for s in SOURCES] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [
+        REPO / "include" / "qi.h", Path(__file__).resolve()]
     newest = max(p.stat().st_mtime for p in deps)
     if LIB.exists() and not force and LIB.stat().st_mtime >= newest:
         return LIB

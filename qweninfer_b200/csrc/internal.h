@@ -77,6 +77,11 @@ struct AttnParams {
 };
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl);
+// Prefill form (attention_block.cu): one CTA per (16 consecutive query tokens, KV head);
+// uses q, kc, vc, pos, rows, M, max_len, cache_rows, out/out_act/out_nt, err.
+cudaError_t launch_attention_block(const AttnParams& p, cudaStream_t stream, bool pdl);
+// Query counts above this run attention_block_kernel (decode batches stay at or below it).
+constexpr int kBlockAttnMinTokens = 128;
 
 // slots (optional): the first n_slots argmax slots are zeroed. norm_w/NT/act/ss (optional,
 // all or none): also emit activation tiles of norm_w * x and per-token sums of squares for

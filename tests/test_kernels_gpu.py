@@ -218,6 +218,67 @@ def test_attention_ragged(M, max_len, positions):
                 assert np.abs(got[t, h * 64:(h + 1) * 64] - ref).max() < 1e-5, (t, h)
 
 
+def _prefill_layout(lens, rows):
+    """A batched prefill's query tokens (DecodeRunner.prefill_many): every prompt's tokens but
+    the last in order, then all prompts' last tokens."""
+    pos = [q for n in lens for q in range(n - 1)] + [n - 1 for n in lens]
+    rws = [r for n, r in zip(lens, rows) for _ in range(n - 1)] + list(rows)
+    return np.array(pos), np.array(rws)
+
+
+PREFILL_CASES = ["one_prompt", "batched", "ragged", "long", "bad_position"]
+
+
+@pytest.mark.parametrize("case", PREFILL_CASES)
+def test_attention_prefill_blocks(case):
+    """More than 128 queries run the block kernel (16 consecutive tokens of one row as one
+    tcgen05 tile, else token by token on CUDA cores) vs an fp64 reference; a query outside
+    the cache is reported and its output left untouched."""
+    from qweninfer_b200.models.qwen2 import _AttnScratch
+    rng = np.random.default_rng(40 + PREFILL_CASES.index(case))
+    max_len, rows_total = 512, 4
+    if case == "one_prompt":
+        pos, rows = np.arange(300), np.full(300, 2)
+    elif case == "batched":
+        pos, rows = _prefill_layout([150, 37, 200, 1], [3, 0, 1, 2])
+    elif case == "ragged":  # every block mixes rows: the token-by-token path
+        pos, rows = rng.integers(0, max_len, 200), rng.integers(0, rows_total, 200)
+    elif case == "long":
+        max_len = 4096
+        pos, rows = _prefill_layout([1100, 700], [1, 3])
+    else:
+        pos, rows = np.arange(160), np.full(160, 1)
+        pos[37] = max_len
+    M = len(pos)
+    kc = bf16_round(rng.standard_normal((rows_total, 2, max_len, 64)).astype(np.float32))
+    vc = bf16_round(rng.standard_normal((rows_total, 2, max_len, 64)).astype(np.float32))
+    q = rng.standard_normal((M, 896)).astype(np.float32) * 2
+    ws = _AttnScratch(M, max_len, torch.device(DEV))
+    out = torch.full((M, 896), 7.0, device=DEV)
+    kcd, vcd = bf16_tensor(kc).to(DEV), bf16_tensor(vc).to(DEV)
+    _lib.check(_lib.lib().qi_attention(
+        f32(q).data_ptr(), kcd.data_ptr(), vcd.data_ptr(), i32(pos).data_ptr(), i32(rows).data_ptr(), M,
+        max_len, ws.split_keys, ws.max_splits, out.data_ptr(), ws.part.data_ptr(), ws.counters.data_ptr(),
+        ws.err.data_ptr(), stream()), "attention")
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    bad = pos >= max_len
+    assert int(ws.err.item()) == (_lib.QI_ERR_INDEX if bad.any() else 0)
+    assert (got[bad] == 7.0).all()
+    qd = q.astype(np.float64).reshape(M, 14, 64)
+    for t in np.flatnonzero(~bad):
+        n = pos[t] + 1
+        for g in range(2):
+            s = qd[t, 7 * g:7 * g + 7] @ kc[rows[t], g, :n].T.astype(np.float64) / 8.0   # (7, n)
+            pr = np.exp(s - s.max(axis=1, keepdims=True))
+            ref = (pr / pr.sum(axis=1, keepdims=True)) @ vc[rows[t], g, :n]
+            err = np.abs(got[t].reshape(14, 64)[7 * g:7 * g + 7] - ref).max()
+            # tensor-core blocks carry q and p as hi + lo bf16 (~16 significant bits, the
+            # precision of the o projection's operand): scores within ~1e-5 relative, and
+            # rows over a few dozen keys, where single terms dominate, within 1e-4
+            assert err < 1e-4, (t, g, err)
+
+
 @pytest.mark.parametrize("M", [1, 4, 11])
 def test_residual_projections(M):
     rng = np.random.default_rng(5)
