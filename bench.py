@@ -17,12 +17,15 @@ Printed JSON (rank 0, one line):
   e2e     the same tokens / time of the window's Engine.step calls through the public
           API (CUDA events around them): host bookkeeping, per-step H2D of (ids,
           positions, rows) from pinned memory and D2H of the argmax words included.
-  roofline  the decode-step kernel (step_kernel: the whole forward of a decode step in
-          one launch) over the window's decode steps: algorithmic bytes per launch
-          (weights + KV read + KV write + embedding rows) / launch time vs the measured
-          HBM copy peak.
-  full_trace, batch1, prefill, serve64_padded  the other BASELINE configurations on the
-          same model (N = 1 only).
+  roofline  the kernel with the largest share of a decode step of the window (each launch
+          of that step timed alone with CUDA events, `kernels` lists them all): algorithmic
+          bytes per launch (weights streamed, KV read or appended, embedding rows) / launch
+          time vs the measured HBM copy peak; step_roofline: the same for the whole step.
+  serve3072  the scaled serving trace (3072 requests, rid % N over N replicas, 128 slots
+          and max_len 4096 per GPU): whole-job tok/s = all output tokens / slowest rank.
+  full_trace, batch1, prefill, serve64_padded  the other benchmark configurations on the
+          same model (N = 1 only): the whole 96-request trace, batch-1 decode at contexts
+          16/256/1024, prefill time to first token, 64 slots with autotuned padding.
   cpu_baseline  the numpy oracle (the reference's algorithm restated) on the host cores
           over a bounded sample of the same window.
 
@@ -76,6 +79,7 @@ def parse():
                     help="one measurement alone (profiling cases): graph-replayed decode steps at --batch, "
                          "config-1 batch-1 decode, config-2 prefill, config-3 64 padded slots")
     ap.add_argument("--batch", type=int, default=22, help="decode batch of --only decode")
+    ap.add_argument("--lengths", default="64,256,512,1024", help="prompt lengths of --only prefill")
     return ap.parse_args()
 
 
@@ -206,6 +210,7 @@ def run_trace(eng, timed: TimedRunner, workload, window=WINDOW) -> dict:
     for r in reqs:
         eng.submit(r)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    timed.reset()  # this run's forwards only
     launches0 = eng.runner.launches
     h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
     out: dict = {}
@@ -444,7 +449,7 @@ def batch1_latency(model, pk: dict) -> dict:
     return out
 
 
-def prefill_ttft(model, pk: dict) -> dict:
+def prefill_ttft(model, pk: dict, lengths=(64, 256, 512, 1024)) -> dict:
     """Config 2: batch-1 causal prefill of seed-3 prompts of 64/256/512/1024 tokens writing
     the cache and emitting the first greedy token; TTFT (CUDA events, median of 5 after a
     warm-up) and the achieved dense rate: 2 * (block params * P + head params) plus the
@@ -454,6 +459,8 @@ def prefill_ttft(model, pk: dict) -> dict:
     from qweninfer_b200.engine.runner import DecodeRunner
     out = {}
     for P, prompt in synthetic.prefill_prompts().items():
+        if P not in lengths:
+            continue
         cache = KVCache(model.cfg, 1, P, dtype=torch.bfloat16, device=model.device)
         r = DecodeRunner(model, cache, max_batch=1)
         r.prefill(0, prompt)
@@ -668,7 +675,8 @@ def main() -> None:
         model = load_model(device)
         pk = peaks()
         r = {"decode": lambda: decode_steps(model, args.batch, args.steps, args.warmup),
-             "batch1": lambda: batch1_latency(model, pk), "prefill": lambda: prefill_ttft(model, pk),
+             "batch1": lambda: batch1_latency(model, pk),
+             "prefill": lambda: prefill_ttft(model, pk, tuple(int(x) for x in args.lengths.split(","))),
              "serve64": lambda: serve64(model)}[args.only]()
         print(json.dumps(r), flush=True)
         return

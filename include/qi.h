@@ -218,14 +218,6 @@ typedef struct {
   long long tc_scratch_floats;
   unsigned int* tc_counters;/* one per output tile, zero-initialised          */
   int tc_counters_len;
-  /* decode step (qi_decode_step) */
-  unsigned int* step_counters; /* phase counters, one 128-byte line (32 uints) per phase:
-                                  step_counters_len >= 32 * (1 + 6 * layers); zeroed by
-                                  each qi_decode_step call                            */
-  int step_counters_len;
-  unsigned long long* step_trace; /* optional (may be NULL): the timeline of each
-                                     qi_decode_step launch, 8 globaltimer stamps (ns) per
-                                     CTA and phase: (148 * 194 * 8) uint64 (see step.h) */
 } qi_workspace;
 
 /* Full Qwen2 forward of M tokens (qweninfer/models/qwen2.py:263-292 with a cache):
@@ -265,27 +257,6 @@ int qi_forward_launch_times(const qi_model* model, const qi_cache* cache, const 
                             long long logits_ld, unsigned long long* argmax_slots,
                             qi_stream_t stream, int* kinds, float* us, int max_launches,
                             int* n_launches);
-
-/* ---------------------------------------------------------- decode step */
-
-/* One batched decode step of M <= 32 rows as ONE cooperative launch (148 CTAs, one per
- * SM, in clusters of 2): embedding, every layer, final norm, tied head and greedy argmax
- * of every token (head tokens 0..M-1). Token t is the next token of cache row rows[t] at
- * position pos[t]; the rows must be distinct (one token per row, as in a decode step:
- * qweninfer/engine/engine.py:140-155 calling Qwen2.forward, qwen2.py:263-292, with S = 1).
- * Same results as qi_forward with head_lo = 0, head_stride = 1, n_head = M, up to fp32
- * summation order. Each CTA streams its share of every layer's weights through a ring of
- * shared-memory slots ahead of the phase that multiplies them; phases (QKV, attention, o,
- * gate/up, down, reduce) wait on global counters in ws->step_counters (>= 32 * (1 + 6 *
- * layers) uints, zeroed by this call). Uses ws->x, q, act_x, act_attn, act_h, ss
- * (ss_ld >= 32), tc_scratch (>= 148*32 + 21*32*896 floats), attn_part, attn_counters,
- * err; split_keys/max_splits as for qi_forward. A position or row outside the cache is
- * reported as QI_ERR_INDEX in *ws->err and that token's cache slot is not written.
- * Returns QI_ERR_DEVICE on a GPU without 148 SMs. */
-int qi_decode_step(const qi_model* model, const qi_cache* cache, const qi_workspace* ws,
-                   const int32_t* ids, const int32_t* pos, const int32_t* rows, int M,
-                   void* logits, int logits_bf16, long long logits_ld,
-                   unsigned long long* argmax_slots, qi_stream_t stream);
 
 /* ------------------------------------------------- tensor-core building blocks */
 

@@ -50,8 +50,7 @@ class QiWorkspace(C.Structure):
                 ("attn_counters", vp), ("max_tokens", i32), ("max_splits", i32),
                 ("split_keys", i32), ("err", vp), ("use_tc", i32), ("act_x", vp), ("act_attn", vp),
                 ("act_h", vp), ("ss", vp), ("ss_ld", i32), ("tc_scratch", vp), ("tc_scratch_floats", i64),
-                ("tc_counters", vp), ("tc_counters_len", i32), ("step_counters", vp), ("step_counters_len", i32),
-                ("step_trace", vp)]
+                ("tc_counters", vp), ("tc_counters_len", i32)]
 
 
 # name -> (restype, argtypes), exactly the declarations of include/qi.h
@@ -72,8 +71,6 @@ SIGNATURES = {
     "qi_move_rows": (i32, [vp, vp, i32, i32, i32, C.POINTER(i32), i32, vp]),
     "qi_forward": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp,
                          i32, i32, i32, i32, vp, i32, i64, vp, vp]),
-    "qi_decode_step": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp, i32, vp,
-                             i32, i64, vp, vp]),
     "qi_forward_launch_times": (i32, [C.POINTER(QiModel), C.POINTER(QiCache), C.POINTER(QiWorkspace), vp, vp, vp,
                                       i32, i32, i32, i32, vp, i32, i64, vp, vp, vp, vp, i32, vp]),
     "qi_act_tiles": (i32, [vp, vp, i32, i32, i32, vp, vp, i32, vp]),

@@ -9,7 +9,6 @@
 #include "common.cuh"
 #include "internal.h"
 #include "tc_proj.h"
-#include "step.h"
 
 #include <map>
 #include <vector>
@@ -545,70 +544,6 @@ bool bad_forward_args(const qi_model* model, const qi_cache* cache, const qi_wor
 }  // namespace
 
 extern "C" {
-
-int qi_decode_step(const qi_model* model, const qi_cache* cache, const qi_workspace* ws, const int32_t* ids,
-                   const int32_t* pos, const int32_t* rows, int M, void* logits, int logits_bf16, long long logits_ld,
-                   unsigned long long* argmax_slots, qi_stream_t stream) {
-  using namespace qi::step;
-  if (!model || !cache || !ws || !model->layers || M <= 0 || M > kMaxTokens || M > ws->max_tokens ||
-      model->num_layers <= 0 || model->num_layers > kMaxLayers || model->vocab % kTileRows != 0 ||
-      bad_ptr(ids) || bad_ptr(pos) || bad_ptr(rows) || bad_ptr(argmax_slots) || (logits && logits_ld < model->vocab) ||
-      ws->split_keys <= 0 || ws->split_keys % 128 != 0 || (long long)ws->split_keys * ws->max_splits < cache->max_len ||
-      ws->max_splits > kMaxAttnSplits || !ws->x || !ws->q || !ws->act_x || !ws->act_attn || !ws->act_h || !ws->ss ||
-      !ws->tc_scratch || !ws->attn_part || !ws->attn_counters || !ws->err || !ws->step_counters)
-    return QI_ERR_ARG;
-  const int NT = M <= 8 ? 8 : M <= 16 ? 16 : 32;
-  if (cache->max_len > model->max_seq || ws->ss_ld < NT || ws->tc_scratch_floats < (long long)kGrid * NT + (long long)kDownRanges * NT * kHidden ||
-      ws->step_counters_len < kCounterStride * (1 + kPhasesPerLayer * model->num_layers))
-    return QI_ERR_ARG;
-  if (!step_supported()) return QI_ERR_DEVICE;
-  StepParams P;
-  memset(&P, 0, sizeof(P));
-  for (int l = 0; l < model->num_layers; ++l) {
-    const qi_layer& L = model->layers[l];
-    P.L[l] = StepLayer{L.w_qkv, L.w_o, L.w_gate_up, L.w_down, L.b_qkv, L.ln1, L.ln2};
-  }
-  P.n_layers = model->num_layers;
-  P.embed = model->embed;
-  P.vocab = model->vocab;
-  P.norm_w = model->norm;
-  P.eps = model->eps;
-  P.rope_cos = model->rope_cos;
-  P.rope_sin = model->rope_sin;
-  P.ids = ids;
-  P.pos = pos;
-  P.rows = rows;
-  P.M = M;
-  P.NT = NT;
-  P.kc = cache->k;
-  P.vc = cache->v;
-  P.layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
-  P.cache_rows = cache->cache_rows;
-  P.max_len = cache->max_len;
-  P.x = ws->x;
-  P.q = ws->q;
-  P.act_x = ws->act_x;
-  P.act_attn = ws->act_attn;
-  P.act_h = ws->act_h;
-  P.ss = ws->ss;
-  P.ss_o = ws->tc_scratch;
-  P.dpart = ws->tc_scratch + (long long)kGrid * NT;
-  P.apart = ws->attn_part;
-  P.acnt = ws->attn_counters;
-  P.split_keys = ws->split_keys;
-  P.max_splits = ws->max_splits;
-  P.ctr = ws->step_counters;
-  P.logits = logits;
-  P.logits_bf16 = logits_bf16;
-  P.logits_ld = logits_ld;
-  P.argmax = argmax_slots;
-  P.err = ws->err;
-  P.trace = ws->step_trace;
-  P.slots = step_ring_slots(NT);
-  P.chains = step_chains(NT);
-  P.tmem_cols = step_tmem_cols(NT);
-  return rc(launch_step(P, as_stream(stream)));
-}
 
 int qi_version(void) { return kVersion; }
 

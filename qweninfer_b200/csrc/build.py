@@ -21,7 +21,7 @@ CSRC = Path(__file__).resolve().parent
 PKG = CSRC.parent
 REPO = PKG.parent
 LIB = PKG / "libqi.so"
-SOURCES = ["gemv.cu", "attention.cu", "attention_block.cu", "misc.cu", "norm_rope.cu", "tc_proj.cu", "step.cu", "api.cu"]
+SOURCES = ["gemv.cu", "attention.cu", "attention_block.cu", "misc.cu", "norm_rope.cu", "tc_proj.cu", "api.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

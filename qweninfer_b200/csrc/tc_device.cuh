@@ -1,5 +1,5 @@
 // Device-side building blocks of the tensor-core kernels (tc_proj.cu, and the tcgen05 /
-// TMEM wrappers and descriptors the decode-step kernel in step.cu uses): UMMA
+// TMEM wrappers and descriptors the prefill attention in attention_block.cu uses): UMMA
 // descriptors, the stream-K partition, activation-tile addressing and the fused
 // epilogues of every projection.
 #pragma once

@@ -18,7 +18,6 @@ import torch
 
 from qweninfer_b200 import _lib
 from qweninfer_b200.engine.kv_cache import KVCache
-from qweninfer_b200.models.qwen2 import use_step
 
 
 class _Staging:
@@ -73,15 +72,7 @@ class DecodeRunner:
 
     # ------------------------------------------------------------ helpers
 
-    def _forward(self, st: _Staging, M: int, ws, head_lo: int, n_head: int, decode: bool = False) -> None:
-        if decode and use_step(M):
-            # the whole step (embedding, every layer, head + argmax) as one launch
-            self.launches += 1
-            _lib.check(_lib.lib().qi_decode_step(
-                C.byref(self.model.native()), C.byref(self.cache.native()), C.byref(ws.struct),
-                st.ptr(0), st.ptr(1), st.ptr(2), M, None, 0, 0, self.d_slots.data_ptr(),
-                _lib.stream_ptr(self.dev)), "qi_decode_step")
-            return
+    def _forward(self, st: _Staging, M: int, ws, head_lo: int, n_head: int) -> None:
         self.launches += self.kernels_per_forward(M)
         _lib.check(_lib.lib().qi_forward(
             C.byref(self.model.native()), C.byref(self.cache.native()), C.byref(ws.struct),
@@ -176,11 +167,11 @@ class DecodeRunner:
             g.replay()
         else:
             self.ws.plan(B)
-            self._forward(self.dec, B, self.ws, 0, B, decode=True)
+            self._forward(self.dec, B, self.ws, 0, B)
             if self.cuda_graphs:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
-                    self._forward(self.dec, B, self.ws, 0, B, decode=True)
+                    self._forward(self.dec, B, self.ws, 0, B)
                 self.graphs[B] = g
         self.steps += 1
         return self._read(B)

@@ -315,17 +315,6 @@ def gate_up_tile(M: int) -> int:
     return 8 if M <= 8 else 32 if M <= 32 else 64 if M <= 384 else 128
 
 
-STEP_MAX_TOKENS = 32
-
-
-def use_step(M: int) -> bool:
-    """A decode step of M <= 32 rows (one token per cache row) as one cooperative launch
-    (`qi_decode_step`) when QI_STEP=1; by default the per-projection launches of
-    `qi_forward`, which measure faster for now."""
-    import os
-    return M <= STEP_MAX_TOKENS and use_tensor_cores() and os.environ.get("QI_STEP", "0") == "1"
-
-
 def use_tensor_cores() -> bool:
     """tcgen05 projections (default) or the CUDA-core GEMV path (QI_TENSOR_CORES=0)."""
     import os
@@ -365,25 +354,13 @@ class Workspace:
         n_counters = max(76 * -(-pad // 8), -(-vocab // 128), 64)  # any token tile down to 8
         self.tc_counters = torch.zeros(n_counters, dtype=torch.int32, device=device)
         # decode-step phase counters: one 128-byte line per phase, 1 + 6 per layer (32 layers)
-        self.step_counters = torch.zeros(32 * (1 + 6 * 32), dtype=torch.int32, device=device)
         self.struct = _lib.QiWorkspace(
             self.x.data_ptr(), self.q.data_ptr(), self.attn.data_ptr(), self.h.data_ptr(),
             self.attn_part.data_ptr(), self.attn_counters.data_ptr(), max_tokens, 1, 128, self.err.data_ptr(),
             int(use_tensor_cores()), self.act_x.data_ptr(), self.act_attn.data_ptr(), self.act_h.data_ptr(),
             self.ss.data_ptr(), pad, self.tc_scratch.data_ptr(), self.tc_scratch.numel(),
-            self.tc_counters.data_ptr(), n_counters, self.step_counters.data_ptr(), self.step_counters.numel(),
-            None)
+            self.tc_counters.data_ptr(), n_counters)
 
-    def trace_steps(self, on: bool = True) -> torch.Tensor | None:
-        """Record the timeline of every following qi_decode_step launch on this workspace
-        (globaltimer stamps per CTA and phase, see csrc/step.h); returns the buffer."""
-        if on:
-            if getattr(self, "step_trace", None) is None:
-                self.step_trace = torch.zeros(148 * 194 * 8, dtype=torch.int64, device=self.x.device)
-            self.struct.step_trace = self.step_trace.data_ptr()
-            return self.step_trace
-        self.struct.step_trace = None
-        return None
 
     def plan(self, M: int) -> "Workspace":
         self.struct.split_keys, self.struct.max_splits = _split_plan(M, self.max_len)
@@ -578,9 +555,16 @@ class Qwen2(nn.Module):
     @classmethod
     def from_pretrained(cls, path: str | Path, dtype: torch.dtype = torch.float16,
                         device: str | torch.device = "cuda", max_seq_len: int = 4096,
-                        fuse: bool = True, residual_fp32: bool = True) -> "Qwen2":
+                        fuse: bool = True, residual_fp32: bool = True,
+                        load_on_device: bool = True) -> "Qwen2":
         """qwen2.py:310-337: meta-device construction, safetensors load (strict), RoPE
-        tables rebuilt in fp32, `fuse()` on the host, then one move to `device`.
+        tables rebuilt in fp32, `fuse()`, on `device`.
+
+        With `load_on_device` (the default for a CUDA `device`) the safetensors tensors are
+        read straight into device memory and the repack into the kernels' tiled layout
+        (`fuse`) runs there as device copies: the host never holds a repacked weight, and
+        the only host work is the file read. Otherwise the repack runs on the host before
+        one move to `device` (the reference's order). Both give identical buffers.
 
         The kernels compute with bfloat16 weights and fp32 activations, whatever `dtype`
         asks for (the reference's default is float16). A float16 or float32 request loads
@@ -592,14 +576,21 @@ class Qwen2(nn.Module):
         if dtype not in (torch.bfloat16, torch.float16, torch.float32):
             raise ValueError(f"dtype must be bfloat16, float16 or float32; got {dtype}")
         path = Path(path)
+        device = torch.device(device)
+        on_dev = load_on_device and device.type == "cuda"
+        if on_dev and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
         cfg = Qwen2Config.from_json(path / "config.json")
         with torch.device("meta"):
             model = cls(cfg, max_seq_len, residual_fp32)
-        state = load_file(path / "model.safetensors", device="cpu")
+        state = load_file(path / "model.safetensors", device=str(device) if on_dev else "cpu")
         state = {k.removeprefix("model."): t.to(dtype).to(torch.bfloat16) for k, t in state.items()}
         model.load_state_dict(state, strict=True, assign=True)
+        del state
         model.rope_cos, model.rope_sin = build_rope_cache(cfg.head_dim, max_seq_len, cfg.rope_theta)
         model.logits_dtype = dtype
+        if on_dev:
+            model.rope_cos, model.rope_sin = model.rope_cos.to(device), model.rope_sin.to(device)
         if fuse:
             model.fuse()
         return model.to(device).eval()

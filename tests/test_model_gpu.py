@@ -244,27 +244,6 @@ def test_forward_writes_only_head_slots(gpu_model):
     assert bool((slots[1:] == sentinel).all())
 
 
-def test_decode_step_writes_only_its_slots(gpu_model):
-    """qi_decode_step zeroes and fills argmax_slots[0..M) only."""
-    import ctypes as C
-    from qweninfer_b200 import _lib
-    M = 5
-    cache = KVCache(gpu_model.cfg, M, 64, dtype=torch.bfloat16, device="cuda")
-    ids = torch.randint(0, gpu_model.cfg.vocab_size, (M,), dtype=torch.int32, device="cuda")
-    pos = torch.zeros(M, dtype=torch.int32, device="cuda")
-    rows = torch.arange(M, dtype=torch.int32, device="cuda")
-    sentinel = 0x0123456789ABCDEF
-    slots = torch.full((M + 8,), sentinel, dtype=torch.int64, device="cuda")
-    ws = gpu_model.workspace(32, 64).plan(M)
-    _lib.check(_lib.lib().qi_decode_step(C.byref(gpu_model.native()), C.byref(cache.native()), C.byref(ws.struct),
-                                         ids.data_ptr(), pos.data_ptr(), rows.data_ptr(), M, None, 0, 0,
-                                         slots.data_ptr(), _lib.stream_ptr(gpu_model.device)), "qi_decode_step")
-    torch.cuda.synchronize()
-    ws.check()
-    assert bool((slots[:M] != sentinel).all())
-    assert bool((slots[M:] == sentinel).all())
-
-
 def test_launch_times_match_the_forward(gpu_model):
     """qi_forward_launch_times runs the same launches as a decode step: embed, 24 x (qkv,
     attention, o, gate/up, down), head, each with a positive time; its greedy tokens equal
@@ -314,3 +293,48 @@ def test_prefill_many_matches_single_prefills(gpu_model):
         # a misplaced token would be O(1)
         err = (a - b).abs().amax(dim=1) / a.abs().amax(dim=1).clamp_min(1e-6)
         assert bool((err <= HIDDEN_RTOL + 2 ** -7).all()), err.max().item()
+
+
+def test_device_load_matches_host_repack(gpu_model, ckpt_bf16):
+    """from_pretrained reading the checkpoint straight into device memory and repacking
+    there gives the same buffers, bit for bit, as the host repack."""
+    from qweninfer_b200.models.qwen2 import Qwen2
+    host = Qwen2.from_pretrained(ckpt_bf16, dtype=torch.bfloat16, device="cuda", load_on_device=False)
+    a = dict(gpu_model.named_buffers()) | dict(gpu_model.named_parameters())
+    b = dict(host.named_buffers()) | dict(host.named_parameters())
+    assert a.keys() == b.keys()
+    for k in a:
+        assert a[k].device.type == "cuda" and a[k].dtype == b[k].dtype and torch.equal(a[k], b[k]), k
+
+
+def test_autotune_padding_table(gpu_model):
+    """autotune_padding (engine.py:199-233): a time for every candidate, pad_to[n] >= n and
+    a candidate for every active count, the fastest candidate >= n; an engine padded with
+    it serves a small trace with the same outputs as the unpadded engine."""
+    from qweninfer_b200.engine.engine import autotune_padding
+    cands = [1, 2, 4, 8, 12, 16]
+    pad_to, ms = autotune_padding(gpu_model, 12, candidates=cands, iters=2)
+    assert set(ms) == set(cands) - {16} | {12} and all(v > 0 for v in ms.values())
+    assert len(pad_to) == 13 and pad_to[0] == 0
+    for n in range(1, 13):
+        ok = [c for c in ms if c >= n]
+        assert pad_to[n] in ok and ms[pad_to[n]] == min(ms[c] for c in ok), n
+    rng = np.random.default_rng(3)
+    reqs = lambda: [Request(i, rng_prompts[i], int(n)) for i, n in enumerate(lens)]  # noqa: E731
+    rng_prompts = [rng.integers(0, gpu_model.cfg.vocab_size, int(p)).tolist() for p in rng.integers(4, 40, 20)]
+    lens = rng.integers(1, 12, 20)
+    plain = Engine(gpu_model, max_slots=12, max_len=64).run(reqs())
+    padded = Engine(gpu_model, max_slots=12, max_len=64, pad_to=pad_to).run(reqs())
+    assert [r.output for r in plain] == [r.output for r in padded]
+
+
+def test_generate_streams_and_stops_on_eos(gpu_model):
+    """generate (generate.py:18-51): on_token sees every emitted token in order; an EOS id
+    stops generation before it is emitted."""
+    prompt = torch.tensor([np.random.default_rng(8).integers(0, gpu_model.cfg.vocab_size, 12).tolist()])
+    seen: list[int] = []
+    full = generate(gpu_model, prompt, 10, on_token=seen.append)
+    assert seen == full and len(full) == 10
+    stop = full[4]
+    cut = generate(gpu_model, prompt, 10, eos_ids={stop})
+    assert cut == full[:full.index(stop)]
