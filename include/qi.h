@@ -218,6 +218,10 @@ typedef struct {
   long long tc_scratch_floats;
   unsigned int* tc_counters;/* one per output tile, zero-initialised          */
   int tc_counters_len;
+  int query_run;            /* longest run of consecutive query tokens of one cache
+                               row in the next forward (a prompt's length), or 0 if
+                               unknown. Attention runs the prefill block kernel when
+                               it is >= 384 (0: when the forward has > 128 tokens)  */
 } qi_workspace;
 
 /* Full Qwen2 forward of M tokens (qweninfer/models/qwen2.py:263-292 with a cache):

@@ -50,7 +50,7 @@ class QiWorkspace(C.Structure):
                 ("attn_counters", vp), ("max_tokens", i32), ("max_splits", i32),
                 ("split_keys", i32), ("err", vp), ("use_tc", i32), ("act_x", vp), ("act_attn", vp),
                 ("act_h", vp), ("ss", vp), ("ss_ld", i32), ("tc_scratch", vp), ("tc_scratch_floats", i64),
-                ("tc_counters", vp), ("tc_counters_len", i32)]
+                ("tc_counters", vp), ("tc_counters_len", i32), ("query_run", i32)]
 
 
 # name -> (restype, argtypes), exactly the declarations of include/qi.h

@@ -92,7 +92,7 @@ bool use_block_attention() {
 int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int32_t* pos, const int32_t* rows,
               int M, int max_len, int split_keys, int max_splits, float* out, float* part, unsigned int* counters,
               int* err, cudaStream_t s, bool pdl, uint16_t* out_act = nullptr, int out_nt = 0,
-              int cache_rows = 0) {
+              int cache_rows = 0, int query_run = 0) {
   if (max_splits > kMaxAttnSplits) return QI_ERR_ARG;
   AttnParams a = {};
   a.out_act = out_act;
@@ -111,9 +111,10 @@ int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int3
   a.part = part;
   a.counters = counters;
   a.err = err;
-  // prefill-sized query counts: blocks of 16 tokens share K/V tiles (a prompt's tokens
-  // are consecutive in the forward)
-  if (M > kBlockAttnMinTokens && use_block_attention()) return rc(launch_attention_block(a, s, pdl));
+  // prompts of kBlockAttnMinRun tokens or more (or, length unknown, prefill-sized query
+  // counts): blocks of 16 consecutive tokens share K/V tiles on the tensor cores
+  if (use_block_attention() && (query_run > 0 ? query_run >= kBlockAttnMinRun : M > kBlockAttnMinTokens))
+    return rc(launch_attention_block(a, s, pdl));
   // splits of a token merged inside a cluster when a launch has 2..8 of them
   a.cluster = (use_tc_clusters() && max_splits >= 2 && max_splits <= 8) ? 1 : 0;
   return rc(launch_attention(a, s, pdl));
@@ -468,7 +469,8 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     prefetch(p, 4 * li);
     if ((r = launch(p, 0)) != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
-                  ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, tiles[1], cache->cache_rows);
+                  ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, tiles[1], cache->cache_rows,
+                  ws->query_run);
     if (r != QI_OK || (r = mark(QI_LAUNCH_ATTENTION)) != QI_OK) return r;
     p = params(1, tiles[2]);  // o_proj + residual; emits RMSNorm(post_attention) inputs
     p.w = L.w_o;

@@ -106,7 +106,7 @@ class DecodeRunner:
         self._check_ids(prompt)
         self.pre.put(prompt, np.arange(P), np.full(P, row), head=P - 1)
         self.h2d_bytes += self.pre.h.numel() * 4
-        ws = self.model.workspace(self.cache.max_len, self.cache.max_len).plan(P)
+        ws = self.model.workspace(self.cache.max_len, self.cache.max_len).plan(P, P)
         self._forward(self.pre, P, ws, P - 1, 1)
         return int(self._read(1)[0])
 
@@ -142,7 +142,7 @@ class DecodeRunner:
             M = len(ids)
             self.pre.put(ids, pos, rws)
             self.h2d_bytes += self.pre.h.numel() * 4
-            ws = self.model.workspace(cap, cap).plan(M)
+            ws = self.model.workspace(cap, cap).plan(M, max(len(p) for p in chunk))
             self._forward(self.pre, M, ws, M - n, n)
             out += [int(t) for t in self._read(n)]
             i = j

@@ -353,17 +353,19 @@ class Workspace:
         self.tc_scratch = torch.empty(sms * 2 * 128 * nt, **f32)
         n_counters = max(76 * -(-pad // 8), -(-vocab // 128), 64)  # any token tile down to 8
         self.tc_counters = torch.zeros(n_counters, dtype=torch.int32, device=device)
-        # decode-step phase counters: one 128-byte line per phase, 1 + 6 per layer (32 layers)
         self.struct = _lib.QiWorkspace(
             self.x.data_ptr(), self.q.data_ptr(), self.attn.data_ptr(), self.h.data_ptr(),
             self.attn_part.data_ptr(), self.attn_counters.data_ptr(), max_tokens, 1, 128, self.err.data_ptr(),
             int(use_tensor_cores()), self.act_x.data_ptr(), self.act_attn.data_ptr(), self.act_h.data_ptr(),
             self.ss.data_ptr(), pad, self.tc_scratch.data_ptr(), self.tc_scratch.numel(),
-            self.tc_counters.data_ptr(), n_counters)
+            self.tc_counters.data_ptr(), n_counters, 0)
 
-
-    def plan(self, M: int) -> "Workspace":
+    def plan(self, M: int, query_run: int = 0) -> "Workspace":
+        """Attention splits for M query tokens; `query_run`: the longest prompt among them
+        (its tokens consecutive and in one cache row), 0 if unknown — it picks the prefill
+        attention kernel."""
         self.struct.split_keys, self.struct.max_splits = _split_plan(M, self.max_len)
+        self.struct.query_run = query_run
         return self
 
     def check(self) -> None:
@@ -512,7 +514,7 @@ class Qwen2(nn.Module):
         ldt = torch.bfloat16 if want == torch.bfloat16 else torch.float32
         logits = torch.empty(n_head, self.cfg.vocab_size, dtype=ldt, device=dev)
         slots = torch.zeros(M, dtype=torch.int64, device=dev)
-        ws = self.workspace(max(M, 1), cache.max_len).plan(M)
+        ws = self.workspace(max(M, 1), cache.max_len).plan(M, S)
         _lib.check(_lib.lib().qi_forward(
             C.byref(self.native()), C.byref(cache.native()), C.byref(ws.struct), ids32.data_ptr(),
             pos32.data_ptr(), rows32.data_ptr(), M, head_lo, head_stride, n_head, logits.data_ptr(),
@@ -530,7 +532,7 @@ class Qwen2(nn.Module):
             raise ValueError(f"n_layers must be in 0..{self.cfg.num_hidden_layers}")
         B, S = input_ids.shape
         cache, M, ids32, pos32, rows32 = self._inputs(input_ids, positions, cache)
-        ws = self.workspace(max(M, 1), cache.max_len).plan(M)
+        ws = self.workspace(max(M, 1), cache.max_len).plan(M, S)
         full = self.native()
         part = _lib.QiModel(n_layers, full.vocab, full.max_seq, full.eps, full.embed, full.norm,
                             full.rope_cos, full.rope_sin, full.layers)
