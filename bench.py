@@ -79,6 +79,8 @@ def parse():
                     help="one measurement alone (profiling cases): graph-replayed decode steps at --batch, "
                          "config-1 batch-1 decode, config-2 prefill, config-3 64 padded slots")
     ap.add_argument("--batch", type=int, default=22, help="decode batch of --only decode")
+    ap.add_argument("--context", type=int, default=200, help="decode positions of --only decode")
+    ap.add_argument("--max-len", type=int, default=512, help="cache slots per row of --only decode")
     ap.add_argument("--lengths", default="64,256,512,1024", help="prompt lengths of --only prefill")
     return ap.parse_args()
 
@@ -399,25 +401,31 @@ def kernel_table(runner, decode_input, pk: dict, reps: int = 5) -> dict:
             "kernels": table}
 
 
-def decode_steps(model, B: int, steps: int, warmup: int) -> dict:
-    """Graph-replayed decode steps of B rows at positions ~200 (the profiling case)."""
+def decode_steps(model, B: int, steps: int, warmup: int, context: int = 200, max_len: int = 512) -> dict:
+    """Graph-replayed decode steps of B rows at positions ~context (row b at context + 7 b
+    mod 1024, so a batch spans contexts context .. context + 1023) in a cache of max_len
+    slots per row: the profiling case."""
     from qweninfer_b200.engine.kv_cache import KVCache
     from qweninfer_b200.engine.runner import DecodeRunner
-    cache = KVCache(model.cfg, B, 512, dtype=torch.bfloat16, device=model.device)
+    cache = KVCache(model.cfg, B, max_len, dtype=torch.bfloat16, device=model.device)
     r = DecodeRunner(model, cache, max_batch=B)
     toks = [1] * B
+    base = [context + (7 * b) % 1024 for b in range(B)] if context > 200 else [context] * B
+    if max(base) + warmup + steps >= max_len:
+        raise ValueError("contexts past the cache")
     for i in range(warmup):
-        r.decode(toks, [200 + i] * B)
+        r.decode(toks, [p + i for p in base])
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for i in range(steps):
-        r.decode(toks, [200 + warmup + i] * B)
+        r.decode(toks, [p + warmup + i for p in base])
     b.record()
     b.synchronize()
     r.check()
     ms = a.elapsed_time(b) / steps
-    byts = step_bytes([200 + warmup + steps // 2] * B)
-    return {"batch": B, "steps": steps, "ms_per_step": ms, "hbm_gbs": byts / (ms / 1e3) / 1e9}
+    byts = step_bytes([p + warmup + steps // 2 for p in base])
+    return {"batch": B, "steps": steps, "context": context, "max_len": max_len, "ms_per_step": ms,
+            "hbm_gbs": byts / (ms / 1e3) / 1e9}
 
 
 def batch1_latency(model, pk: dict) -> dict:
@@ -674,7 +682,7 @@ def main() -> None:
     if args.only is not None:
         model = load_model(device)
         pk = peaks()
-        r = {"decode": lambda: decode_steps(model, args.batch, args.steps, args.warmup),
+        r = {"decode": lambda: decode_steps(model, args.batch, args.steps, args.warmup, args.context, args.max_len),
              "batch1": lambda: batch1_latency(model, pk),
              "prefill": lambda: prefill_ttft(model, pk, tuple(int(x) for x in args.lengths.split(","))),
              "serve64": lambda: serve64(model)}[args.only]()

@@ -278,12 +278,13 @@ class Block(nn.Module):
 # ------------------------------------------------------------- scratch space
 
 def _split_plan(max_tokens: int, max_len: int) -> tuple[int, int]:
-    """Key-split size and count for attention over `max_len` cache slots. Few queries
-    (decode, M <= 64) must fill 148 SMs: 128 keys per split while that gives at most 8
-    splits, whose merge then runs inside one thread-block cluster (serving bench: decode
-    step 1.19 -> 1.12 ms against 256-key splits), else 256 (measured best over 128/256/512
-    with the merge through global scratch). Prefill-sized M: 1024."""
-    split = (128 if -(-max_len // 128) <= 8 else 256) if max_tokens <= 64 else 1024
+    """Key-split size and count for attention over `max_len` cache slots. Decode batches
+    (M <= 128) must fill 148 SMs: 128 keys per split while that gives at most 8 splits,
+    whose merge then runs inside one thread-block cluster (serving bench: decode step 1.19
+    -> 1.12 ms against 256-key splits), else 256 (measured best over 128/256/512/1024 with
+    the merge through global scratch: batch-128 decode at contexts 128..3000 3.80 -> 3.41
+    ms against 1024). Prefill-sized M: 1024."""
+    split = (128 if -(-max_len // 128) <= 8 else 256) if max_tokens <= 128 else 1024
     import os
     if os.environ.get("QI_ATTN_SPLIT"):  # tuning experiments: keys per split for every M
         split = max(128, int(os.environ["QI_ATTN_SPLIT"]) // 128 * 128)
@@ -332,9 +333,9 @@ class Workspace:
         self.q = torch.empty(max_tokens, HIDDEN, **f32)
         self.attn = torch.empty(max_tokens, HIDDEN, **f32)
         self.h = torch.empty(max_tokens, INTER, **f32)
-        small = min(max_tokens, 64)
+        small = min(max_tokens, 128)
         s_small, n_small = _split_plan(small, max_len)
-        s_big, n_big = _split_plan(max(max_tokens, 65), max_len)
+        s_big, n_big = _split_plan(max(max_tokens, 129), max_len)
         parts = max(small * n_small, max_tokens * n_big) * 2 * 7 * 66
         self.attn_part = torch.empty(parts, **f32)
         self.attn_counters = torch.zeros(max_tokens * 2, dtype=torch.int32, device=device)

@@ -13,7 +13,7 @@ from qweninfer_b200.models.qwen2 import _split_plan, gate_up_tile, token_tile
 
 
 @pytest.mark.parametrize("max_len", [1, 96, 128, 129, 512, 1000, 1024, 1025, 2048, 4096, 32768])
-@pytest.mark.parametrize("M", [1, 22, 64, 65, 512])
+@pytest.mark.parametrize("M", [1, 22, 64, 65, 128, 129, 512])
 def test_split_plan_covers_every_key(M, max_len):
     split, n = _split_plan(M, max_len)
     assert split % 128 == 0 and split >= 128
@@ -22,15 +22,21 @@ def test_split_plan_covers_every_key(M, max_len):
     assert n <= 128  # the merge's capacity
 
 
+@pytest.mark.parametrize("M", [1, 22, 128])
 @pytest.mark.parametrize("max_len", [96, 256, 512, 1024])
-def test_decode_splits_fit_one_cluster(max_len):
-    split, n = _split_plan(22, max_len)
+def test_decode_splits_fit_one_cluster(M, max_len):
+    split, n = _split_plan(M, max_len)
     assert split == 128 and n <= 8
+
+
+@pytest.mark.parametrize("M", [1, 64, 128])
+def test_long_context_decode_splits(M):
+    assert _split_plan(M, 4096) == (256, 16)
 
 
 def test_prefill_splits_are_coarse():
     assert _split_plan(512, 512) == (1024, 1)
-    assert _split_plan(65, 4096)[0] == 1024
+    assert _split_plan(129, 4096)[0] == 1024
 
 
 @pytest.mark.parametrize("rule", [token_tile, gate_up_tile])
