@@ -25,7 +25,6 @@ struct AttnSmem {
   uint16_t v[2][kTile * kHeadDim];
   float q[kGqa * 2 * 8 * 4];          // per head: [half][chunk][4], scaled by 1/sqrt(64)
   float p[4][32][8];                  // per key group: probabilities of its 32 keys, 7 heads
-  float cmb[4][kGqa][kHeadDim + 2];   // per key group and head: acc[64], m, l
   uint64_t bar[2];
   int last;
 };
@@ -229,16 +228,20 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     if (tid < 8 && i + 2 < ntiles) issue(i + 2);
   }
 
-  // Merge the 4 key groups.
+  // Merge the 4 key groups. Their partials (acc[64], m, l per key group and head) take the
+  // place of K tile 0, whose last reader was the loop above: the CTA's shared memory then
+  // fits three CTAs per SM.
+  float (&cmb)[4][kGqa][kHeadDim + 2] = *reinterpret_cast<float (*)[4][kGqa][kHeadDim + 2]>(&S.k[0][0]);
+  static_assert(sizeof(float) * 4 * kGqa * (kHeadDim + 2) <= sizeof(S.k[0]), "key-group partials fit a K tile");
 #pragma unroll
   for (int hi = 0; hi < HPG; ++hi) {
     if (hi < nh) {
       const int h = h0 + hi;
-      S.cmb[kgrp][h][2 * lane] = acc[hi][0];
-      S.cmb[kgrp][h][2 * lane + 1] = acc[hi][1];
+      cmb[kgrp][h][2 * lane] = acc[hi][0];
+      cmb[kgrp][h][2 * lane + 1] = acc[hi][1];
       if (lane == 0) {
-        S.cmb[kgrp][h][kHeadDim] = m[hi];
-        S.cmb[kgrp][h][kHeadDim + 1] = l[hi];
+        cmb[kgrp][h][kHeadDim] = m[hi];
+        cmb[kgrp][h][kHeadDim + 1] = l[hi];
       }
     }
   }
@@ -258,15 +261,15 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     const int d = idx - h * (kHeadDim + 2);
     float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, S.cmb[w][h][kHeadDim]);
+    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, cmb[w][h][kHeadDim]);
     float L = 0.f, A = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const float mw = S.cmb[w][h][kHeadDim];
+      const float mw = cmb[w][h][kHeadDim];
       if (mw == -INFINITY) continue;
       const float sc = expf(mw - mx);
-      L = fmaf(sc, S.cmb[w][h][kHeadDim + 1], L);
-      if (d < kHeadDim) A = fmaf(sc, S.cmb[w][h][d], A);
+      L = fmaf(sc, cmb[w][h][kHeadDim + 1], L);
+      if (d < kHeadDim) A = fmaf(sc, cmb[w][h][d], A);
     }
     const float val = d < kHeadDim ? A : (d == kHeadDim ? mx : L);
     if (nsplit == 1) {
@@ -306,7 +309,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   // (1) every split's running max and sum into shared memory (reusing the warp-merge
   // area: 2 * 7 * nsplit + 7 floats), (2) per head the max and the split weights
   // exp(m_s - max), (3) the weighted sum of the split outputs, loads before stores.
-  float* sm = &S.cmb[0][0][0];
+  float* sm = &cmb[0][0][0];
   for (int idx = tid; idx < kGqa * nsplit; idx += NT) {
     const int h = idx / nsplit, s = idx - h * nsplit;
     const float mv = load(s, h * (kHeadDim + 2) + kHeadDim), lv = load(s, h * (kHeadDim + 2) + kHeadDim + 1);
