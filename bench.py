@@ -561,7 +561,7 @@ def serve3072(model, rank: int, world: int, device: torch.device, pk: dict) -> d
     if rank != 0:
         return None
     tokens = float(sm[2])
-    gbs = float(sm[3]) / (float(sm[4]) / 1e3) / 1e9 / world
+    gbs = float(sm[3]) / (float(sm[4]) / 1e3) / 1e9  # bytes and device time summed over the ranks
     return {"workload": "serve3072: 3072 requests (prompts U[128,2048], outputs lognormal(200,0.9)<=1024, seed 5), "
                         f"rid % {world} over {world} replica(s), {slots} slots and max_len {max_len} per GPU",
             "value": tokens / (float(mx[0]) / 1e3), "unit": "tok/s", "scaling": "strong",
