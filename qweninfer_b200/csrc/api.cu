@@ -226,17 +226,18 @@ void token_tiles(int M, int nt[4]) {
   for (int i = 0; i < 4; ++i) nt[i] = env[i] ? env[i] : (i == 2 ? gu : t);
 }
 
-// Shared-memory budget of a tensor-core projection CTA for its pipeline stages, in KB
-// (QI_TC_SMEM_KB overrides the default of 144 for tuning experiments; 144 KB measured best
-// across decode batches 1-64 and prefill).
-int tc_smem_budget_kb() {
+// Shared-memory budget of a tensor-core projection CTA for its pipeline stages, in KB, by
+// token tile: 144 for decode-sized tiles (<= 32; measured best over 96-192 at batches
+// 1-64), 192 for prefill-sized ones (1024-token prefill 4.80 -> 4.59 ms against 144).
+// QI_TC_SMEM_KB overrides both for tuning experiments.
+int tc_smem_budget_kb(int NT) {
   static int kb = -1;
   if (kb < 0) {
     const char* s = getenv("QI_TC_SMEM_KB");
     const int v = s ? atoi(s) : 0;
-    kb = (v >= 48 && v <= 220) ? v : 144;
+    kb = (v >= 48 && v <= 220) ? v : 0;
   }
-  return kb;
+  return kb > 0 ? kb : (NT <= 32 ? 144 : 192);
 }
 
 // Stream-K contributor caps of the forward's projections (qkv, o, gate/up, down, head):
@@ -308,7 +309,7 @@ int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* c
   // Deep pipelines: a CTA streams at (bytes in flight) / (loaded DRAM latency, ~3 us), so
   // ~130 KB must be in flight per SM to reach the HBM rate.
   const size_t stage = 16384 + (size_t)p.NT * 256;
-  int stages = (int)((size_t)tc_smem_budget_kb() * 1024 / stage);
+  int stages = (int)((size_t)tc_smem_budget_kb(p.NT) * 1024 / stage);
   stages = stages < 2 ? 2 : (stages > 12 ? 12 : stages);
   // Split tiles on thread-block clusters when every tile has the same number C (2..8) of
   // contributors: the partials then travel through distributed shared memory instead of a
