@@ -185,10 +185,20 @@ typedef struct {
 } qi_model;
 
 typedef struct {
-  uint16_t* k;              /* (layers, cache_rows, 2, max_len, 64) bf16 */
+  uint16_t* k;              /* (layers, cache_rows, 2, max_len, 64) bf16, or paged */
   uint16_t* v;
   int cache_rows;
   int max_len;
+  /* Paged layout when page_table is not NULL (no reference counterpart: its cache is packed):
+   * k and v are pools of n_pages pages per layer, (layers, n_pages, 2, page_size, 64) bf16;
+   * page_table[row * pages_per_row + pos / page_size] (device int32, cache_rows x
+   * pages_per_row) is the page holding position pos of cache row `row`, -1 if unmapped
+   * (reported as QI_ERR_INDEX). page_size is a multiple of 128 and pages_per_row *
+   * page_size >= max_len. Only qi_forward with ws->use_tc reads a paged cache. */
+  const int32_t* page_table;
+  int page_size;
+  int pages_per_row;
+  int n_pages;
 } qi_cache;
 
 typedef struct {

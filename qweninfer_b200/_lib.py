@@ -42,7 +42,8 @@ class QiModel(C.Structure):
 
 
 class QiCache(C.Structure):
-    _fields_ = [("k", vp), ("v", vp), ("cache_rows", i32), ("max_len", i32)]
+    _fields_ = [("k", vp), ("v", vp), ("cache_rows", i32), ("max_len", i32), ("page_table", vp),
+                ("page_size", i32), ("pages_per_row", i32), ("n_pages", i32)]
 
 
 class QiWorkspace(C.Structure):

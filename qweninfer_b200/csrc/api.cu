@@ -92,7 +92,7 @@ bool use_block_attention() {
 int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int32_t* pos, const int32_t* rows,
               int M, int max_len, int split_keys, int max_splits, float* out, float* part, unsigned int* counters,
               int* err, cudaStream_t s, bool pdl, uint16_t* out_act = nullptr, int out_nt = 0,
-              int cache_rows = 0, int query_run = 0) {
+              int cache_rows = 0, int query_run = 0, KvLayout kv = KvLayout{}) {
   if (max_splits > kMaxAttnSplits) return QI_ERR_ARG;
   AttnParams a = {};
   a.out_act = out_act;
@@ -111,6 +111,7 @@ int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int3
   a.part = part;
   a.counters = counters;
   a.err = err;
+  a.kv = kv;
   // prompts of kBlockAttnMinRun tokens or more (or, length unknown, prefill-sized query
   // counts): blocks of 16 consecutive tokens share K/V tiles on the tensor cores
   if (use_block_attention() && (query_run > 0 ? query_run >= kBlockAttnMinRun : M > kBlockAttnMinTokens))
@@ -363,6 +364,26 @@ int grid_for(int n_tiles, int KB, int max_contrib) {
 // qi_forward on the tensor-core path: every projection is a tc_proj launch whose
 // epilogue writes the next projection's activation tiles (the RMSNorm weights folded in,
 // the per-token RMS applied in the consumer's epilogue from partial sums of squares).
+// The cache's KV layout and the elements one layer's K (or V) takes.
+KvLayout kv_layout(const qi_cache* c) {
+  KvLayout kv = {};
+  if (c->page_table) {
+    kv.table = c->page_table;
+    kv.page = c->page_size;
+    kv.ppr = c->pages_per_row;
+    kv.n_pages = c->n_pages;
+  }
+  return kv;
+}
+long long layer_kv_elems(const qi_cache* c) {
+  return c->page_table ? (long long)c->n_pages * kKvHeads * c->page_size * kHeadDim
+                       : (long long)c->cache_rows * kKvHeads * c->max_len * kHeadDim;
+}
+bool bad_paging(const qi_cache* c) {
+  return c->page_table && (c->page_size < 128 || c->page_size % 128 != 0 || c->n_pages < 1 ||
+                           (long long)c->pages_per_row * c->page_size < c->max_len);
+}
+
 // Per-launch device times of one forward: an event recorded before the first launch and
 // after every launch (qi_forward_launch_times). The events separate the launches, so each
 // time is the launch's own duration without the programmatic-dependent-launch overlap.
@@ -445,18 +466,20 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     const int r = run_tc(p, ws->tc_scratch, ws->tc_scratch_floats, ws->tc_counters, ws->tc_counters_len, g, s, pdl);
     return r != QI_OK ? r : mark(kinds[j]);
   };
-  const long long layer_elems = (long long)cache->cache_rows * kKvHeads * cache->max_len * kHeadDim;
+  const KvLayout kv = kv_layout(cache);
+  const long long layer_elems = layer_kv_elems(cache);
   for (int li = 0; li < model->num_layers; ++li) {
     const qi_layer& L = model->layers[li];
     uint16_t* kl = cache->k + li * layer_elems;
     uint16_t* vl = cache->v + li * layer_elems;
     TcParams p = params(0, 0);  // RMSNorm + QKV + bias + RoPE + KV append
+    p.kv = kv;
     p.w = L.w_qkv;
     p.KB = kHidden / 64;
     p.n_mtiles = kQkvRows / 128;
     p.act_in = ws->act_x;
     p.ss_in = ws->ss;
-    p.epi = kTcQkvRope;
+    p.epi = cache->page_table ? kTcQkvRopePaged : kTcQkvRope;
     p.bias = L.b_qkv;
     p.rope_cos = model->rope_cos;
     p.rope_sin = model->rope_sin;
@@ -471,7 +494,7 @@ int forward_tc(const qi_model* model, const qi_cache* cache, const qi_workspace*
     if ((r = launch(p, 0)) != QI_OK) return r;
     r = attention(ws->q, kl, vl, pos, rows, M, cache->max_len, ws->split_keys, ws->max_splits, nullptr,
                   ws->attn_part, ws->attn_counters, ws->err, s, pdl, ws->act_attn, tiles[1], cache->cache_rows,
-                  ws->query_run);
+                  ws->query_run, kv);
     if (r != QI_OK || (r = mark(QI_LAUNCH_ATTENTION)) != QI_OK) return r;
     p = params(1, tiles[2]);  // o_proj + residual; emits RMSNorm(post_attention) inputs
     p.w = L.w_o;
@@ -715,7 +738,8 @@ int qi_forward(const qi_model* model, const qi_cache* cache, const qi_workspace*
                void* logits, int logits_bf16, long long logits_ld, unsigned long long* argmax_slots,
                qi_stream_t stream) {
   if (bad_forward_args(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits, logits_ld,
-                       argmax_slots))
+                       argmax_slots) ||
+      bad_paging(cache) || (cache->page_table && !ws->use_tc))
     return QI_ERR_ARG;
   if (ws->use_tc) return forward_tc(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits,
                                     logits_bf16, logits_ld, argmax_slots, as_stream(stream));
@@ -755,7 +779,7 @@ int qi_forward_launch_times(const qi_model* model, const qi_cache* cache, const 
                             int max_launches, int* n_launches) {
   if (bad_forward_args(model, cache, ws, ids, pos, rows, M, head_lo, head_stride, n_head, logits, logits_ld,
                        argmax_slots) ||
-      !ws->use_tc || !kinds || !us || !n_launches || max_launches <= 0)
+      bad_paging(cache) || !ws->use_tc || !kinds || !us || !n_launches || max_launches <= 0)
     return QI_ERR_ARG;
   LaunchTimer lt;
   lt.s = as_stream(stream);

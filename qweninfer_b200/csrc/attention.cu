@@ -26,6 +26,7 @@ using namespace attn;
 
 constexpr size_t kMergeOffset = (sizeof(AttnSmem) + 15) / 16 * 16;
 
+template <bool kPaged>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
@@ -50,7 +51,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   if (cm) cluster_arrive();
   uint32_t uses[2] = {0u, 0u};
   bool waited = false;
-  attention_unit<false, 8>(p, S, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, uses, cm, &waited);
+  attention_unit<false, 8, kPaged>(p, S, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, uses, cm, &waited);
   if (cm && !waited) cluster_wait();
 }
 
@@ -58,7 +59,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl) {
   const size_t smem_max = kMergeOffset + sizeof(ClusterMerge);
-  cudaError_t e = set_max_dynamic_smem(reinterpret_cast<const void*>(attention_kernel), (int)smem_max);
+  const bool paged = p.kv.table != nullptr;
+  const void* fn = paged ? reinterpret_cast<const void*>(attention_kernel<true>)
+                         : reinterpret_cast<const void*>(attention_kernel<false>);
+  cudaError_t e = set_max_dynamic_smem(fn, (int)smem_max);
   if (e != cudaSuccess) return e;
   if (p.cluster && (p.max_splits < 2 || p.max_splits > kMaxClusterSplits)) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
@@ -80,7 +84,7 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl)
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, attention_kernel, p);
+  return paged ? cudaLaunchKernelEx(&cfg, attention_kernel<true>, p) : cudaLaunchKernelEx(&cfg, attention_kernel<false>, p);
 }
 
 

@@ -75,6 +75,14 @@ constexpr int kSliceV = kChunk * kHeadDim * 2;
 constexpr int kSliceBytes = kSliceQ + kSliceV + kGqa * kChunk * 4;
 static_assert(4 * kSliceBytes <= 32768, "token slices fit the P area");
 
+// K/V offset of (row, head g, first key k0 of a tile or chunk); an unmapped page is
+// reported and read from the layer's start (in bounds)
+__device__ __forceinline__ long long kv_base(const AttnParams& p, int row, int g, int k0) {
+  const long long o = kv_offset(p.kv, p.max_len, row, g, k0);
+  if (o < 0 && p.err) atomicExch(p.err, QI_ERR_INDEX);
+  return o < 0 ? 0 : o;
+}
+
 // One tile's K and V (keys k0 .. k0 + nk - 1 of a row's head) as 4 + 4 16-byte chunks per
 // thread: chunk q = tid + 128 j is key 8 (q >> 6) + (q & 7), dims 8 ((q >> 3) & 7) ..; keys
 // past nk read as zeros. The 8 lanes of a store phase hold 8 keys of one chunk column.
@@ -82,16 +90,16 @@ struct TileRegs {
   uint4 k[4], v[4];
 };
 
-__device__ __forceinline__ void tile_load(TileRegs& R, const uint16_t* kg, const uint16_t* vg, int k0, int nk,
-                                          int tid) {
+// kt / vt: the tile's first key (a tile never straddles a page)
+__device__ __forceinline__ void tile_load(TileRegs& R, const uint16_t* kt, const uint16_t* vt, int nk, int tid) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int q = tid + 128 * j;
     const int n = ((q >> 6) << 3) | (q & 7), c = (q >> 3) & 7;
     if (n < nk) {
-      const long long o = (long long)(k0 + n) * kHeadDim + c * 8;
-      R.k[j] = __ldcg(reinterpret_cast<const uint4*>(kg + o));
-      R.v[j] = __ldcg(reinterpret_cast<const uint4*>(vg + o));
+      const long long o = (long long)n * kHeadDim + c * 8;
+      R.k[j] = __ldcg(reinterpret_cast<const uint4*>(kt + o));
+      R.v[j] = __ldcg(reinterpret_cast<const uint4*>(vt + o));
     } else {
       R.k[j] = R.v[j] = make_uint4(0u, 0u, 0u, 0u);
     }
@@ -146,9 +154,6 @@ __device__ __forceinline__ void token_path(const AttnParams& p, uint8_t* smem, c
       }
       __syncwarp();
     }
-    const long long head_base = (((long long)X.row[j] * kKvHeads + g) * p.max_len) * kHeadDim;
-    const uint16_t* kg = p.kc + head_base;
-    const uint16_t* vg = p.vc + head_base;
     float m[kGqa], l[kGqa], acc[kGqa][2];
 #pragma unroll
     for (int h = 0; h < kGqa; ++h) {
@@ -159,8 +164,9 @@ __device__ __forceinline__ void token_path(const AttnParams& p, uint8_t* smem, c
     for (int k0 = 0; k0 <= ps; k0 += kChunk) {
       const int key = k0 + lane;
       const bool valid = key <= ps;
-      const uint4* krow = reinterpret_cast<const uint4*>(kg + (long long)(valid ? key : k0) * kHeadDim);
-      const uint4* vrow = reinterpret_cast<const uint4*>(vg + (long long)(valid ? key : k0) * kHeadDim);
+      const long long cb = kv_base(p, X.row[j], g, k0) + (long long)(valid ? lane : 0) * kHeadDim;
+      const uint4* krow = reinterpret_cast<const uint4*>(p.kc + cb);
+      const uint4* vrow = reinterpret_cast<const uint4*>(p.vc + cb);
       // V chunks in rotated order (vx[c] = chunk (c + lane) & 7), so the stores of the 8
       // lanes of a phase hit distinct banks
       uint4 kx[8], vx[8];
@@ -265,14 +271,16 @@ __device__ __forceinline__ void tc_segment(const AttnParams& p, uint8_t* smem, M
       *reinterpret_cast<uint4*>(smem + kQlo + kmaj(tid, c)) = lo[c];
     }
   }
-  const long long head_base = (((long long)X.seg_row[sg] * kKvHeads + g) * p.max_len) * kHeadDim;
-  const uint16_t* kg = p.kc + head_base;
-  const uint16_t* vg = p.vc + head_base;
+  const int srow = X.seg_row[sg];
+  auto load = [&](TileRegs& T, int k0, int nk) {
+    const long long o = kv_base(p, srow, g, k0);
+    tile_load(T, p.kc + o, p.vc + o, nk, tid);
+  };
   const int ntiles = (kmax + kKT - 1) / kKT;
   TileRegs R;
-  tile_load(R, kg, vg, 0, min(kKT, kmax), tid);
+  load(R, 0, min(kKT, kmax));
   tile_store(R, smem, 0, tid);
-  if (ntiles > 1) tile_load(R, kg, vg, kKT, min(kKT, kmax - kKT), tid);
+  if (ntiles > 1) load(R, kKT, min(kKT, kmax - kKT));
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -302,7 +310,7 @@ __device__ __forceinline__ void tc_segment(const AttnParams& p, uint8_t* smem, M
     // tile i + 2 requested
     if (i + 1 < ntiles) {
       tile_store(R, smem, b ^ 1, tid);
-      if (i + 2 < ntiles) tile_load(R, kg, vg, k0 + 2 * kKT, min(kKT, kmax - k0 - 2 * kKT), tid);
+      if (i + 2 < ntiles) load(R, k0 + 2 * kKT, min(kKT, kmax - k0 - 2 * kKT));
     }
     const uint32_t par = b ? (nb_s1++ & 1u) : (nb_s0++ & 1u);
     mbar_wait(&X.bar_s[b], par, p.err);

@@ -54,7 +54,7 @@ __device__ __forceinline__ void emit(const AttnParams& p, int tok, int f, float 
 // cm: the cluster merge buffer (standalone kernel with AttnParams::cluster), else null;
 // *waited is set when the unit waited on the cluster barrier (a split that pushes its
 // partial to split 0 does so before its first remote store).
-template <bool kNamedBarrier, int NW>
+template <bool kNamedBarrier, int NW, bool kPaged = false>
 __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S, int split, int g, int tok,
                                                int tid, uint32_t (&uses)[2], ClusterMerge* cm = nullptr,
                                                bool* waited = nullptr) {
@@ -84,9 +84,19 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   if (split >= nsplit) return false;
   const int kbeg = split * p.split_keys;
   const int kend = min(nkeys, kbeg + p.split_keys);
+  // tile i's keys start at K/V offset tile_base(k0): packed, one run per (row, head);
+  // paged, a tile never straddles a page, and an unmapped page is reported and read from
+  // the layer's start (in bounds)
   const long long head_base = (((long long)row * kKvHeads + g) * p.max_len) * kHeadDim;
-  const uint16_t* kg = p.kc + head_base;
-  const uint16_t* vg = p.vc + head_base;
+  auto tile_base = [&](int k0) -> long long {
+    if constexpr (!kPaged) {
+      return head_base + (long long)k0 * kHeadDim;
+    } else {
+      const long long o = kv_offset(p.kv, p.max_len, row, g, k0);
+      if (o < 0 && p.err) atomicExch(p.err, QI_ERR_INDEX);
+      return o < 0 ? 0 : o;
+    }
+  };
 
   const int ntiles = (kend - kbeg + kTile - 1) / kTile;
   // mbarrier phases continue across the units a CTA runs: tile i uses stage i & 1
@@ -106,9 +116,9 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     const int q = tid & 3, kq = (nk + 3) >> 2;
     const int a = min(nk, q * kq), b = min(nk, a + kq);
     if (b > a) {
-      const long long o = (long long)(k0 + a) * kHeadDim;
-      if (tid < 4) bulk_g2s(S.k[st] + a * kHeadDim, kg + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
-      else bulk_g2s(S.v[st] + a * kHeadDim, vg + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
+      const long long o = tile_base(k0) + (long long)a * kHeadDim;
+      if (tid < 4) bulk_g2s(S.k[st] + a * kHeadDim, p.kc + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
+      else bulk_g2s(S.v[st] + a * kHeadDim, p.vc + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
     }
   };
   // the first two tiles are requested before q is staged: the copies do not depend on

@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include "../../include/qi.h"
+#include "kv_layout.h"
 
 namespace qi {
 
@@ -40,6 +41,15 @@ __host__ __device__ __forceinline__ long long tiled_group_offset(int group, int 
 
 __host__ __device__ __forceinline__ long long tiled_offset(int n, int k, int K) {
   return tiled_group_offset(n >> 3, k >> 6, K) + ((k & 63) >> 3) * 64 + (n & 7) * 8 + (k & 7);
+}
+
+// Element offset of (row, KV head g, position pos) within one layer's K or V (KvLayout),
+// or -1 when the position's page is unmapped.
+__device__ __forceinline__ long long kv_offset(const KvLayout& L, int max_len, int row, int g, int pos) {
+  if (!L.table) return (((long long)row * kKvHeads + g) * max_len + pos) * kHeadDim;
+  const int pg = __ldg(L.table + (long long)row * L.ppr + pos / L.page);
+  if (pg < 0 || pg >= L.n_pages) return -1;
+  return (((long long)pg * kKvHeads + g) * L.page + pos % L.page) * kHeadDim;
 }
 
 // --------------------------------------------------------------- conversions

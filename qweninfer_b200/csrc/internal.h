@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "kv_layout.h"
+
 namespace qi {
 
 // Key splits per query token that the attention split merge supports.
@@ -63,6 +65,7 @@ struct AttnParams {
   int M;
   int max_len;
   int cache_rows;  // rows of the cache (0: rows are not checked)
+  KvLayout kv;     // packed (kv.table == nullptr) or paged cache
   int split_keys;
   int max_splits;
   float* out;         // fp32 (M, 896), may be null

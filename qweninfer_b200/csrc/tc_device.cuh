@@ -244,6 +244,8 @@ struct ChunkPre<kTcQkvRope, CT> {
   float cs[CT], sn[CT], b;
 };
 template <int CT>
+struct ChunkPre<kTcQkvRopePaged, CT> : ChunkPre<kTcQkvRope, CT> {};
+template <int CT>
 struct ChunkPre<kTcResidual, CT> {
   float xo[CT], wn;
 };
@@ -253,7 +255,7 @@ struct ChunkPre<kTcResidual, CT> {
 template <int EPI, int CT>
 __device__ __forceinline__ void pre_load(const TcParams& p, int n, int tbase, int nlive, const int* tpos,
                                          const int* trow, ChunkPre<EPI, CT>& pre) {
-  if constexpr (EPI == kTcQkvRope) {
+  if constexpr (kIsQkv<EPI>) {
     const int head = n >> 6, j = (n & 63) >> 1;
     const bool rope = head < kHeads + kKvHeads;
     pre.b = __ldg(p.bias + n);
@@ -286,7 +288,7 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
 #pragma unroll
     for (int i = 0; i < CT; ++i)
       if (i < nlive) p.out[(long long)(tbase + i) * p.out_ld + n] = v[i] * rs[i];
-  } else if constexpr (EPI == kTcQkvRope) {
+  } else if constexpr (kIsQkv<EPI>) {
     // bias, RoPE (qwen2.py:160-171, 86-99), q out / KV append (kv_cache.py:59-60)
     const int head = n >> 6, half = n & 1, d = ((n & 63) >> 1) + 32 * half;
     const bool rope = head < kHeads + kKvHeads;
@@ -305,6 +307,10 @@ __device__ __forceinline__ void finish_rows(const TcParams& p, int n, int tbase,
         const int t = tbase + i;
         if (head < kHeads) {
           p.q[(long long)t * kHidden + head * kHeadDim + d] = x[i];
+        } else if constexpr (EPI == kTcQkvRopePaged) {
+          const long long o = kv_slot_ok(p, tpos[i], trow[i]) ? kv_offset(p.kv, p.max_len, trow[i], kvh, tpos[i]) : -1;
+          if (o >= 0) kvbase[o + d] = f32_to_bf16_rn(x[i]);
+          else if (d == 0 && p.err) atomicExch(p.err, QI_ERR_INDEX);
         } else if (kv_slot_ok(p, tpos[i], trow[i])) {
           kvbase[(((long long)trow[i] * kKvHeads + kvh) * p.max_len + tpos[i]) * kHeadDim + d] = f32_to_bf16_rn(x[i]);
         } else if (d == 0 && p.err) {
@@ -386,7 +392,7 @@ __device__ __forceinline__ void warm_params(const TcParams& p) {
   asm volatile("" ::"l"(p.scratch), "l"(p.counters), "r"(p.cluster), "l"(p.err), "r"(p.M), "r"(p.n_ntiles),
                "r"(p.ntile0));
   if constexpr (EPI == kTcPlain) asm volatile("" ::"l"(p.out), "r"(p.out_ld));
-  if constexpr (EPI == kTcQkvRope)
+  if constexpr (kIsQkv<EPI>)
     asm volatile("" ::"l"(p.q), "l"(p.kc), "l"(p.vc), "r"(p.max_len), "r"(p.cache_rows));
   if constexpr (EPI == kTcResidual)
     asm volatile("" ::"l"(p.x), "l"(p.act_out), "r"(p.out_nt), "r"(p.lg_out_nt), "l"(p.ss_out), "r"(p.ss_ld));
@@ -444,7 +450,7 @@ __device__ __forceinline__ void epilogue_range(const TcParams& p, const Geom& ge
           r = 1.0f / sqrtf(ss / (float)kHidden + p.eps);
         }
         es.rsm[et] = r;
-        if constexpr (EPI == kTcQkvRope) {
+        if constexpr (kIsQkv<EPI>) {
           es.tpos[et] = et < live ? __ldg(p.pos + tok0 + et) : 0;
           es.trow[et] = et < live ? __ldg(p.rows + tok0 + et) : 0;
         }

@@ -240,6 +240,7 @@ cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, boo
   switch (p.epi) {
     case kTcPlain: kern = tc_proj_kernel<kTcPlain>; break;
     case kTcQkvRope: kern = tc_proj_kernel<kTcQkvRope>; break;
+    case kTcQkvRopePaged: kern = tc_proj_kernel<kTcQkvRopePaged>; break;
     case kTcResidual: kern = tc_proj_kernel<kTcResidual>; break;
     case kTcSwiglu: kern = tc_proj_kernel<kTcSwiglu>; break;
     case kTcLogits: kern = tc_proj_kernel<kTcLogits>; break;
@@ -272,6 +273,7 @@ cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, boo
 
 int tc_proj_max_clusters(int epi, int NT, int stages, int cluster) {
   void (*kern)(TcParams) = epi == kTcQkvRope    ? tc_proj_kernel<kTcQkvRope>
+                           : epi == kTcQkvRopePaged ? tc_proj_kernel<kTcQkvRopePaged>
                            : epi == kTcResidual ? tc_proj_kernel<kTcResidual>
                            : epi == kTcSwiglu   ? tc_proj_kernel<kTcSwiglu>
                            : epi == kTcLogits   ? tc_proj_kernel<kTcLogits>

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "kv_layout.h"
+
 namespace qi {
 
 enum TcEpilogue : int {
@@ -12,7 +14,12 @@ enum TcEpilogue : int {
   kTcResidual = 2,  // x[t, n] += D; next activations hi/lo(w_next * x) + sum-of-squares partials
   kTcSwiglu = 3,    // h = silu(gate) * up -> activation tiles of the down projection
   kTcLogits = 4,    // optional logits + packed argmax of the head tokens
+  kTcQkvRopePaged = 5,  // kTcQkvRope into a paged cache (TcParams::kv)
 };
+
+// the QKV epilogue kinds (packed or paged KV append)
+template <int EPI>
+constexpr bool kIsQkv = EPI == kTcQkvRope || EPI == kTcQkvRopePaged;
 
 // Activation tiles: for inner size K and token tile NT (8..128, power of two), token t,
 // column k, half `part` (0 = hi = bf16(x), 1 = lo = bf16(x - hi)):
@@ -54,6 +61,7 @@ struct TcParams {
   uint16_t* vc;
   int max_len;
   int cache_rows;  // rows of the cache (0: rows are not checked)
+  KvLayout kv;     // packed (kv.table == nullptr) or paged cache
   // residual / swiglu
   float* x;
   const float* next_norm_w;

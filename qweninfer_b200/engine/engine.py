@@ -22,7 +22,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from qweninfer_b200.engine.kv_cache import KVCache
+from qweninfer_b200.engine.kv_cache import KVCache, PagedKVCache
 from qweninfer_b200.engine.runner import DecodeRunner
 
 
@@ -52,17 +52,24 @@ class Engine:
     def __init__(self, model, max_slots: int, max_len: int, eos_ids: set[int] | None = None,
                  static: bool = False, max_prefills_per_step: int | None = None,
                  pad_to: list[int] | None = None, cuda_graphs: bool = True,
-                 record: bool = False, batch_prefill: bool = True) -> None:
+                 record: bool = False, batch_prefill: bool = True, page_size: int = 0,
+                 kv_pages: int | None = None) -> None:
         """engine.py:62-98. Extra keywords: `cuda_graphs` (capture each decode batch size),
-        `record` (keep a per-step trace of scheduler actions in `self.trace`) and
-        `batch_prefill` (prefill a step's admissions together; same decisions)."""
+        `record` (keep a per-step trace of scheduler actions in `self.trace`),
+        `batch_prefill` (prefill a step's admissions together; same decisions) and
+        `page_size` (> 0: a PagedKVCache of pages of that many positions, `kv_pages` pages
+        per layer; row moves then move page-table entries; same decisions)."""
         if pad_to is not None:
             if len(pad_to) <= max_slots or any(pad_to[n] < n for n in range(max_slots + 1)):
                 raise ValueError("pad_to needs an entry n -> size >= n for n = 0..max_slots")
         rows = max([max_slots] + (pad_to[: max_slots + 1] if pad_to else []))
         self.model = model
         self.device = model.norm.weight.device
-        self.cache = self.cache_cls(model.cfg, rows, max_len, dtype=model.dtype, device=self.device)
+        if page_size:
+            self.cache = PagedKVCache(model.cfg, rows, max_len, dtype=model.dtype, device=self.device,
+                                      page_size=page_size, n_pages=kv_pages)
+        else:
+            self.cache = self.cache_cls(model.cfg, rows, max_len, dtype=model.dtype, device=self.device)
         self.max_slots, self.max_len = max_slots, max_len
         self.eos_ids = eos_ids or set()
         self.static = static
@@ -82,6 +89,13 @@ class Engine:
                              f" tokens, capacity is {self.max_len}")
         req.arrival = req.arrival or time.perf_counter()
         self.waiting.append(req)
+
+    def _release(self, row: int) -> None:
+        """A row's request is gone: a paged cache takes its pages back (a cache without
+        storage management, like the packed one, has nothing to do)."""
+        release = getattr(self.cache, "release", None)
+        if release is not None:
+            release(row)
 
     def _finish_check(self, req: Request, tok: int) -> bool:
         """engine.py:109-113."""
@@ -125,6 +139,7 @@ class Engine:
                 if self._finish_check(req, tok):
                     req.finished = req.first_token
                     done.append(req)
+                    self._release(row)  # the next admission reuses the row
                     continue
                 req.length, req.last = len(req.prompt), tok
                 self.active.append(req)
@@ -168,6 +183,8 @@ class Engine:
                 if self._rec is not None:
                     self._rec["move"].append([last, row, mover.length])
                 self.active[row] = mover
+            else:
+                self._release(row)
             self.active.pop()
             done.append(req)
         return done

@@ -17,7 +17,7 @@ import numpy as np
 import torch
 
 from qweninfer_b200 import _lib
-from qweninfer_b200.engine.kv_cache import KVCache
+from qweninfer_b200.engine.kv_cache import KVCache, PagedKVCache
 
 
 class _Staging:
@@ -69,10 +69,14 @@ class DecodeRunner:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.kernels_per_forward = lambda M: 1 + 5 * model.cfg.num_hidden_layers + 1
+        # a paged cache maps pages before each forward; packed rows need nothing
+        self.paged = isinstance(cache, PagedKVCache)
 
     # ------------------------------------------------------------ helpers
 
     def _forward(self, st: _Staging, M: int, ws, head_lo: int, n_head: int) -> None:
+        if self.paged:
+            self.cache.sync()  # new page-table entries, before the kernels read them
         self.launches += self.kernels_per_forward(M)
         _lib.check(_lib.lib().qi_forward(
             C.byref(self.model.native()), C.byref(self.cache.native()), C.byref(ws.struct),
@@ -104,6 +108,8 @@ class DecodeRunner:
         if not 0 <= row < self.cache.max_batch:
             raise IndexError(f"cache row {row} outside 0..{self.cache.max_batch - 1}")
         self._check_ids(prompt)
+        if self.paged:
+            self.cache.reserve(row, P)
         self.pre.put(prompt, np.arange(P), np.full(P, row), head=P - 1)
         self.h2d_bytes += self.pre.h.numel() * 4
         ws = self.model.workspace(self.cache.max_len, self.cache.max_len).plan(P, P)
@@ -127,6 +133,9 @@ class DecodeRunner:
             if not 0 <= row < self.cache.max_batch:
                 raise IndexError(f"cache row {row} outside 0..{self.cache.max_batch - 1}")
             self._check_ids(p)
+        if self.paged:
+            for row, p in zip(rows, prompts):
+                self.cache.reserve(row, len(p))
         out: list[int] = []
         i = 0
         while i < len(prompts):
@@ -160,6 +169,12 @@ class DecodeRunner:
         if max(pos) >= self.cache.max_len or min(pos) < 0:
             raise IndexError(f"position outside 0..{self.cache.max_len - 1}")
         self._check_ids(toks)
+        if self.paged:
+            for b, q in enumerate(pos):
+                self.cache.reserve(row_start + b, int(q) + 1)
+            # page-table changes go out before the step, graph replays included (nothing is
+            # left to copy when a graph is captured, so no copy is recorded into it)
+            self.cache.sync()
         self.dec.put(toks, pos, np.arange(row_start, row_start + B))
         self.h2d_bytes += self.dec.h.numel() * 4
         g = self.graphs.get(B)
@@ -186,6 +201,10 @@ class DecodeRunner:
         if max(pos) >= self.cache.max_len or min(pos) < 0:
             raise IndexError(f"position outside 0..{self.cache.max_len - 1}")
         self._check_ids(toks)
+        if self.paged:
+            for b, q in enumerate(pos):
+                self.cache.reserve(row_start + b, int(q) + 1)
+            self.cache.sync()
         self.dec.put(toks, pos, np.arange(row_start, row_start + B))
         self.ws.plan(B)
         cap = 8 * (2 + 5 * self.model.cfg.num_hidden_layers)

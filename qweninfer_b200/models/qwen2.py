@@ -471,7 +471,7 @@ class Qwen2(nn.Module):
         synchronisation, as in the reference's forward): the kernels check every position
         and cache row and clamp token ids, and record QI_ERR_INDEX in the workspace error
         word (`check()`) instead of touching memory outside the cache."""
-        from qweninfer_b200.engine.kv_cache import KVCache
+        from qweninfer_b200.engine.kv_cache import KVCache, PagedKVCache
         dev = self.device
         _lib.ensure_device(dev)
         B, S = input_ids.shape
@@ -491,6 +491,14 @@ class Qwen2(nn.Module):
         if input_ids.device.type == "cpu":
             if int(input_ids.min()) < 0 or int(input_ids.max()) >= self.cfg.vocab_size:
                 raise IndexError("token id outside the vocabulary")
+        if isinstance(cache, PagedKVCache):
+            # a paged cache maps the pages of the positions this forward writes and reads
+            if positions.device.type != "cpu":
+                raise ValueError("a paged KV cache needs the positions on the host")
+            last = positions.reshape(B, S).max(dim=1).values
+            for b in range(B):
+                cache.reserve(cache.row_start + b, int(last[b]) + 1)
+            cache.sync()
         ids32 = input_ids.reshape(M).to(device=dev, dtype=torch.int32, non_blocking=True).contiguous()
         pos32 = positions.reshape(M).to(device=dev, dtype=torch.int32, non_blocking=True).contiguous()
         rows32 = (cache.row_start + torch.arange(B, device=dev, dtype=torch.int32)).repeat_interleave(S)
