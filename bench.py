@@ -597,12 +597,14 @@ def cpu_threads() -> int:
     return n
 
 
-def oracle_window(n_steps: int, samples: int, warmup: int) -> dict:
-    """The numpy oracle (the reference's fp32 algorithm) on the host cores: the serving
-    trace (32 slots) is brought to engine step WINDOW[0] by the scheduler's bookkeeping
-    alone (no arithmetic; the KV prefix rows stay zero, which changes no operation count),
-    then `n_steps` engine steps are timed with full arithmetic from that state, `samples`
-    times (after `warmup` untimed single steps). Returns tokens per second."""
+def oracle_window(slice_steps: int, samples: int, warmup: int, slices: int = 1) -> dict:
+    """The numpy oracle (the reference's fp32 algorithm) on the host cores over the timed
+    window of the serving trace (32 slots), in slices of `slice_steps` engine steps: slice
+    j starts at engine step WINDOW[0] + j * slice_steps, a state reached by the scheduler's
+    bookkeeping alone (no arithmetic; the cache stays zero, which changes no operation
+    count). Sample i runs slice i % slices with full arithmetic from its start state; with
+    slices * slice_steps = the window's length, samples cycle through the whole window.
+    Returns output tokens per second over all samples (after `warmup` untimed steps)."""
     from oracle import OracleModel, OracleRequest, bf16_round
     from oracle.engine_ref import OracleEngine, StubModel
     from qweninfer_b200 import synthetic
@@ -618,27 +620,31 @@ def oracle_window(n_steps: int, samples: int, warmup: int) -> dict:
     eng.model = StubModel(cfg.vocab_size)
     for _ in range(WINDOW[0]):
         eng.step()
+    # the scheduler's queues at the start of every slice (the cache is all zero there)
+    starts = []
+    for _ in range(slices):
+        starts.append(copy.deepcopy((list(eng.waiting), list(eng.active))))
+        for _ in range(slice_steps):
+            if eng.waiting or eng.active:
+                eng.step()
     eng.model = oracle
-    # every sample starts from the same state: the cache and the scheduler's queues
-    snap_k, snap_v = eng.cache.k.copy(), eng.cache.v.copy()
-    snap_q = copy.deepcopy((list(eng.waiting), list(eng.active)))
 
-    def restore() -> list:
-        eng.cache.k[...] = snap_k
-        eng.cache.v[...] = snap_v
-        w, a = copy.deepcopy(snap_q)
+    def restore(j: int) -> list:
+        eng.cache.k[...] = 0.0
+        eng.cache.v[...] = 0.0
+        w, a = copy.deepcopy(starts[j])
         eng.waiting, eng.active = deque(w), a
         return w + a
 
     for _ in range(warmup):
-        restore()
+        restore(0)
         eng.step()
     per = []
-    for _ in range(samples):
-        live = restore()
+    for i in range(samples):
+        live = restore(i % slices)
         t0 = sum(len(r.output) for r in live)
         s0 = time.perf_counter()
-        for _ in range(n_steps):
+        for _ in range(slice_steps):
             if not (eng.waiting or eng.active):
                 break
             eng.step()
@@ -646,17 +652,19 @@ def oracle_window(n_steps: int, samples: int, warmup: int) -> dict:
         per.append((sum(len(r.output) for r in live) - t0, dt))
     toks = sum(t for t, _ in per)
     secs = sum(d for _, d in per)
+    last = WINDOW[0] + slices * slice_steps - 1
     return {"value": toks / secs, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"engine steps {WINDOW[0]}-{WINDOW[0] + n_steps - 1} of the 96-request trace (32 slots) "
-                      f"through the numpy oracle (fp32, {threads} host threads), {samples} sample(s), "
-                      f"{toks // samples} output tokens and {secs / samples:.1f} s each; the state at step "
-                      f"{WINDOW[0]} reached by bookkeeping alone"}
+            "sample": f"engine steps {WINDOW[0]}-{last} of the 96-request trace (32 slots) in {slices} slice(s) "
+                      f"of {slice_steps} steps, {samples} sample(s) cycling through them, through the numpy "
+                      f"oracle (fp32, {threads} host threads), {toks / samples:.0f} output tokens and "
+                      f"{secs / samples:.1f} s per sample; slice starts reached by bookkeeping alone"}
 
 
 def reference_arm(args, rank: int, world: int) -> None:
     if rank != 0:
         return
-    r = oracle_window(WINDOW[1] - WINDOW[0], max(1, args.steps), args.warmup)
+    # one step = a 10-engine-step slice of the window; the steps cycle through its 6 slices
+    r = oracle_window(10, max(1, args.steps), args.warmup, slices=(WINDOW[1] - WINDOW[0]) // 10)
     line = {"impl": "reference", "metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
