@@ -112,6 +112,9 @@ int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int3
   a.counters = counters;
   a.err = err;
   a.kv = kv;
+  // query_run 1: a decode step (one query token per cache row, keys below it cached by
+  // earlier forwards); the kernel then starts its copies before the previous launch ends
+  a.decode = query_run == 1 ? 1 : 0;
   // prompts of kBlockAttnMinRun tokens or more (or, length unknown, prefill-sized query
   // counts): blocks of 16 consecutive tokens share K/V tiles on the tensor cores
   if (use_block_attention() && (query_run > 0 ? query_run >= kBlockAttnMinRun : M > kBlockAttnMinTokens))

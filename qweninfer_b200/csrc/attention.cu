@@ -3,14 +3,12 @@
 // One CTA per (key split, KV head, query token). A query at position p reads only keys
 // 0..p of its own cache row (the reference reads B x window keys and masks). The CTA's
 // key range streams through a two-stage shared-memory ring in 128-key tiles (K and V,
-// 16 KB each, bulk-copied from the packed cache, where one head's keys are contiguous).
-// The 7 query heads of the KV group share every tile: 4 warps each take 32 keys of a
-// tile, compute all 7 scores per key (lane = key), run an fp32 online softmax per warp,
-// and accumulate P.V with lane = 2 output dims. Warps and splits are merged with the
-// usual max-rescaled sums, in split order: with 2-8 splits per launch the splits of a
-// token/head form one thread-block cluster and merge in split 0's shared memory;
-// otherwise the last CTA of a token/head (atomic arrival count) merges them from global
-// scratch and resets its counter.
+// 16 KB each, cp.async from the packed or paged cache); the 7 query heads of the KV group
+// are the rows of warp-level tensor-core MMAs over every tile (attention_device.cuh).
+// Splits are merged with the usual max-rescaled sums, in split order: with 2-8 splits
+// per launch the splits of a token/head form one thread-block cluster and merge in split
+// 0's shared memory; otherwise the last CTA of a token/head (atomic arrival count) merges
+// them from global scratch and resets its counter.
 #include <mutex>
 
 #include "common.cuh"
@@ -31,27 +29,27 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
   ClusterMerge* cm = p.cluster ? reinterpret_cast<ClusterMerge*>(smem_raw + kMergeOffset) : nullptr;
-  grid_dep_wait();
-  grid_dep_launch();
-  if (threadIdx.x == 0) {
-    mbar_init(&S.bar[0], 1);
-    mbar_init(&S.bar[1], 1);
-    if (cm) {
-      // split 0 waits for one arrival per thread of each other split of its token
-      const int ps = p.pos[blockIdx.z];
-      const int nsplit = (ps >= 0 && ps < p.max_len) ? (ps + p.split_keys) / p.split_keys : 1;
-      mbar_init(&cm->bar, (uint32_t)(nsplit > 1 ? (nsplit - 1) * kAttnThreads : 1));
-    }
+  // decode steps read positions and rows (written before the forward) without waiting for
+  // the previous launch; otherwise they may be its outputs
+  if (!p.decode) {
+    grid_dep_wait();
+    grid_dep_launch();
+  }
+  const int tok = blockIdx.z;
+  const int ps = p.pos[tok], row = p.rows[tok];
+  if (cm && threadIdx.x == 0) {
+    // split 0 waits for one arrival per thread of each other split of its token
+    const int nsplit = (ps >= 0 && ps < p.max_len) ? (ps + p.split_keys) / p.split_keys : 1;
+    mbar_init(&cm->bar, (uint32_t)(nsplit > 1 ? (nsplit - 1) * kAttnThreads : 1));
     fence_barrier_init();
   }
   __syncthreads();
-  // Cluster handshake: every thread arrives once the barriers are initialised and waits
+  // Cluster handshake: every thread arrives once the barrier is initialised and waits
   // before its first remote access (the splits that push, inside the unit) or before it
   // ends (all others), so no CTA waits for it up front.
   if (cm) cluster_arrive();
-  uint32_t uses[2] = {0u, 0u};
   bool waited = false;
-  attention_unit<false, 8, kPaged>(p, S, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, uses, cm, &waited);
+  attention_unit<kPaged>(p, S, blockIdx.x, blockIdx.y, tok, ps, row, threadIdx.x, cm, &waited);
   if (cm && !waited) cluster_wait();
 }
 

@@ -1,11 +1,30 @@
-// One attention work unit — (key split, KV head, query token) — as a device function of
-// the standalone attention kernel (attention.cu). NW warps run a unit: warp w takes keys
-// 32*(w % 4).. of every 128-key tile and, with NW = 8, half of the 7 query heads (w / 4
-// picks the half). With one CTA per SM the per-warp chain of dependent shared-memory
-// loads, FMAs and shuffles sets the tile time, so the kernel uses 8 warps (NW = 4 runs all
-// heads per warp, with `sync` a named barrier of those 4 warps when kNamedBarrier is set;
-// otherwise the whole CTA). The two K/V stage mbarriers are initialised once per CTA;
-// `uses` carries their phase counts from unit to unit.
+// One attention work unit — (key split, KV head, query token) — of the ragged decode
+// attention kernel (attention.cu), on the tensor cores with warp-level mma.sync.
+//
+// The 7 query heads of a KV group are the rows of an m16n8k16 A operand: row h holds
+// bf16(q_h) and row h + 8 holds bf16(q_h - bf16(q_h)) (row 7 and 15 are zero), so one
+// MMA multiplies both halves and the thread that owns row h also owns row h + 8: adding
+// the two accumulator rows restores ~16 mantissa bits of the fp32 query with fp32
+// accumulation. The probabilities go back into the same A layout (p_hi in row h, p_lo in
+// row h + 8) for O += P V, straight from the score accumulators, without leaving the
+// registers. 8 warps: warp w takes keys 16w .. 16w + 15 of every 128-key tile (two
+// 8-key n-tiles), keeps its own fp32 online softmax per head (m, l over its keys) and its
+// own O (16 x 64 fp32 accumulators); the warps and then the key splits are merged with
+// max-rescaled sums.
+//
+// K and V tiles are copied with cp.async (16 bytes per thread and copy) into shared
+// memory rows of 128 bytes whose 16-byte chunks are XOR-swizzled by the key index
+// (chunk c of key r sits at c ^ (r & 7)), so the ldmatrix reads of 8 keys at one chunk
+// hit 8 different bank groups: K through ldmatrix (B of S = Q K^T, keys as columns), V
+// through ldmatrix.trans (B of O = P V). Two stages; the copies of tile i + 2 are issued
+// after tile i.
+//
+// Decode steps (AttnParams::decode: every query token is the only one of its cache row in
+// the forward) read the positions and cache rows and copy the first two tiles' cached keys
+// (positions < the query's own) before the programmatic-launch wait: those were written by
+// earlier forwards. Only the query and the key at the query's own position, which the
+// preceding QKV launch writes, are read after it. Key splits without keys end before the
+// wait, so they do not hold SM slots while the previous kernel runs.
 #pragma once
 
 #include "common.cuh"
@@ -15,23 +34,23 @@
 namespace qi {
 namespace attn {
 
-constexpr int kAttnThreads = 256;  // the standalone kernel (NW = 8)
-constexpr int kTile = 128;  // keys per stage
+constexpr int kAttnThreads = 256;  // 8 warps
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kTile = 128;                         // keys per stage
+constexpr int kWarpKeys = kTile / kAttnWarps;      // 16 keys of a tile per warp
 constexpr int kPartStride = kGqa * (kHeadDim + 2);  // floats per (token, head, split) partial
-static_assert(2 * kGqa * kMaxAttnSplits + kGqa <= 4 * kGqa * (kHeadDim + 2), "split merge scratch");
+static_assert(kWarpKeys == 16, "two 8-key n-tiles per warp");
+static_assert(2 * kGqa * kMaxAttnSplits + kGqa <= kAttnWarps * kGqa * (kHeadDim + 2), "split merge scratch");
 
 struct AttnSmem {
-  uint16_t k[2][kTile * kHeadDim];
+  uint16_t k[2][kTile * kHeadDim];  // swizzled rows (see above)
   uint16_t v[2][kTile * kHeadDim];
-  float q[kGqa * 2 * 8 * 4];          // per head: [half][chunk][4], scaled by 1/sqrt(64)
-  float p[4][32][8];                  // per key group: probabilities of its 32 keys, 7 heads
-  uint64_t bar[2];
   int last;
 };
 
-// Split merge in a thread-block cluster (standalone kernel, AttnParams::cluster): the
-// partials of splits 0.. of one (token, KV head) in split 0's shared memory, and the
-// barrier that the other splits' threads arrive on once theirs is stored.
+// Split merge in a thread-block cluster (AttnParams::cluster): the partials of splits 0..
+// of one (token, KV head) in split 0's shared memory, and the barrier that the other
+// splits' threads arrive on once theirs is stored.
 constexpr int kMaxClusterSplits = 8;
 struct ClusterMerge {
   float recv[kMaxClusterSplits][kPartStride];
@@ -49,30 +68,68 @@ __device__ __forceinline__ void emit(const AttnParams& p, int tok, int f, float 
   }
 }
 
+// {bf16(a) in the low half, bf16(b) in the high half}
+__device__ __forceinline__ uint32_t bf16x2(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+// hi/lo halves of the pair (a, b): hi = bf16(x), lo = bf16(x - hi)
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = bf16x2(a, b);
+  lo = bf16x2(a - bf16lo(hi), b - bf16hi(hi));
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// 16-byte asynchronous copy global -> shared; src_bytes 0 writes zeros (nothing is read)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// byte offset of (key r, 16-byte chunk c) in a swizzled tile
+__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
 // Runs unit (split, g, tok); returns true when it wrote the final output of (tok, g)
 // (a single split, or the last split to arrive, which merges all of them).
-// cm: the cluster merge buffer (standalone kernel with AttnParams::cluster), else null;
-// *waited is set when the unit waited on the cluster barrier (a split that pushes its
-// partial to split 0 does so before its first remote store).
-template <bool kNamedBarrier, int NW, bool kPaged = false>
-__device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S, int split, int g, int tok,
-                                               int tid, uint32_t (&uses)[2], ClusterMerge* cm = nullptr,
-                                               bool* waited = nullptr) {
-  static_assert(NW == 4 || NW == 8, "4 or 8 warps");
-  static_assert(!kNamedBarrier || NW == 4, "the named barrier spans 4 warps");
-  constexpr int NT = NW * 32;
-  constexpr int HPG = NW == 4 ? kGqa : (kGqa + 1) / 2;  // heads per warp
-  auto sync = [] {
-    if constexpr (kNamedBarrier) asm volatile("bar.sync 1, 128;" ::: "memory");
-    else __syncthreads();
-  };
+// cm: the cluster merge buffer (AttnParams::cluster), else null; *waited is set when the
+// unit waited on the cluster barrier (a split that pushes its partial to split 0 does so
+// before its first remote store). `ps` and `row` are the query's position and cache row.
+// With p.decode == 0 the caller has taken the programmatic-launch wait before reading
+// them; with p.decode == 1 it is taken here, after the first two tiles' cached keys are
+// requested, and units without keys return without it.
+template <bool kPaged = false>
+__device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S, int split, int g, int tok, int ps,
+                                               int row, int tid, ClusterMerge* cm, bool* waited) {
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int kgrp = warp & 3;                // key group: keys 32 * kgrp .. of each tile
-  const int h0 = (warp >> 2) * HPG;         // first head of this warp
-  const int nh = min(HPG, kGqa - h0);       // heads of this warp
-  const int ps = p.pos[tok];
-  const int row = p.rows[tok];
+  const int gq = lane >> 2;  // accumulator row (head) of this thread, and row + 8
+  const int qd = lane & 3;   // its column pair
+  const bool early = p.decode != 0;
+  auto dep_wait = [&] {
+    grid_dep_wait();
+    grid_dep_launch();
+  };
   if (ps < 0 || ps >= p.max_len || row < 0 || (p.cache_rows > 0 && row >= p.cache_rows)) {
     // outside the cache: reported, nothing read or written; split 0 still counts the
     // (token, head) as finished for callers that wait on completions
@@ -84,6 +141,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   if (split >= nsplit) return false;
   const int kbeg = split * p.split_keys;
   const int kend = min(nkeys, kbeg + p.split_keys);
+  const int ntiles = (kend - kbeg + kTile - 1) / kTile;
   // tile i's keys start at K/V offset tile_base(k0): packed, one run per (row, head);
   // paged, a tile never straddles a page, and an unmapped page is reported and read from
   // the layer's start (in bounds)
@@ -97,165 +155,174 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
       return o < 0 ? 0 : o;
     }
   };
-
-  const int ntiles = (kend - kbeg + kTile - 1) / kTile;
-  // mbarrier phases continue across the units a CTA runs: tile i uses stage i & 1
-  const uint32_t u0s = uses[0], u1s = uses[1];
-  uses[0] += (uint32_t)((ntiles + 1) >> 1);
-  uses[1] += (uint32_t)(ntiles >> 1);
-  auto parity = [&](int i) { return (uint32_t)((((i & 1) ? u1s : u0s) + (uint32_t)(i >> 1)) & 1u); };
-  // Tile i's K and V rows as 8 bulk copies (4 key quarters x K/V), one per thread
-  // 0..7: the copies one thread issues are processed one after another, so a single
-  // issuing thread would serialise them.
-  auto issue = [&](int i) {
+  const uint32_t sk0 = smem_u32(&S.k[0][0]), sv0 = smem_u32(&S.v[0][0]);
+  constexpr uint32_t kStageBytes = kTile * kHeadDim * 2;
+  // Tile i into stage i & 1: keys k0 + r for r < min(nk, lim - k0) are copied; V rows
+  // nk .. (the rest of the last warp's 16 keys) are zero-filled so that P = 0 never meets
+  // a stale non-finite value. 8 chunks of 16 bytes per thread (K then V, key-major).
+  auto issue = [&](int i, int lim) {
     const int k0 = kbeg + i * kTile;
     const int nk = min(kTile, kend - k0);
-    const int st = i & 1;
-    if (tid == 0) mbar_arrive_expect_tx(&S.bar[st], (uint32_t)nk * kHeadDim * 2 * 2);
-    __syncwarp(0xffu);
-    const int q = tid & 3, kq = (nk + 3) >> 2;
-    const int a = min(nk, q * kq), b = min(nk, a + kq);
-    if (b > a) {
-      const long long o = tile_base(k0) + (long long)a * kHeadDim;
-      if (tid < 4) bulk_g2s(S.k[st] + a * kHeadDim, p.kc + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
-      else bulk_g2s(S.v[st] + a * kHeadDim, p.vc + o, (uint32_t)(b - a) * kHeadDim * 2, &S.bar[st]);
+    const int ncopy = min(nk, lim - k0);
+    const int nzero = (nk + kWarpKeys - 1) / kWarpKeys * kWarpKeys;
+    const long long base = tile_base(k0);
+    const uint32_t st = (uint32_t)(i & 1) * kStageBytes;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = tid + j * kAttnThreads;  // 0 .. 2047
+      const int isv = c >> 10, r = (c >> 3) & (kTile - 1), ch = c & 7;
+      const uint16_t* src = (isv ? p.vc : p.kc) + base + (long long)r * kHeadDim + ch * 8;
+      const uint32_t dst = (isv ? sv0 : sk0) + st + swz(r, ch);
+      if (r < ncopy) cp_async16(dst, src, 16u);
+      else if (isv && r >= nk && r < nzero) cp_async16(dst, p.vc + base, 0u);
     }
   };
-  // the first two tiles are requested before q is staged: the copies do not depend on
-  // it, so their latency overlaps the q loads
-  if (tid < 8) {
-    issue(0);
-    if (ntiles > 1) issue(1);
+
+  if (early) {
+    issue(0, ps);
+    cp_async_commit();
+    if (ntiles > 1) issue(1, ps);
+    cp_async_commit();
+    dep_wait();
+    // the key at the query's own position, written by the preceding launch, if its tile
+    // was requested above (the last split's last tile when that is tile 0 or 1)
+    const int it = (ps - kbeg) / kTile;
+    if (kend == nkeys && it < 2 && tid < 16) {
+      const int r = ps - kbeg - it * kTile, isv = tid >> 3, ch = tid & 7;
+      const long long base = tile_base(kbeg + it * kTile);
+      cp_async16((isv ? sv0 : sk0) + (uint32_t)(it & 1) * kStageBytes + swz(r, ch),
+                 (isv ? p.vc : p.kc) + base + (long long)r * kHeadDim + ch * 8, 16u);
+    }
+    cp_async_commit();
+  } else {
+    issue(0, kend);
+    cp_async_commit();
+    if (ntiles > 1) issue(1, kend);
+    cp_async_commit();
   }
 
-  // q of the 7 heads sharing KV head g, pre-scaled by 1/8 (exact), laid out so that the
-  // eight 8-dim chunks' first halves are 16-byte neighbours (conflict-free rotated reads).
-  // (all four loads of a thread are issued before its shared-memory stores)
+  // A operand: q of head gq (hi row gq, lo row gq + 8) pre-scaled by 1/8 (exact), per
+  // 16-dim k-step s: columns 2qd, 2qd + 1 and 2qd + 8, 2qd + 9
+  uint32_t qa[4][4];
   {
-    constexpr int kRounds = (kGqa * kHeadDim + NT - 1) / NT;
-    float qv[kRounds];
+    const float* qrow = p.q + (long long)tok * kHidden + (g * kGqa + (gq < kGqa ? gq : 0)) * kHeadDim + 2 * qd;
+    float2 x[8];
 #pragma unroll
-    for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * NT;
-      qv[r] = __ldcg(p.q + (long long)tok * kHidden + g * kGqa * kHeadDim + (idx < kGqa * kHeadDim ? idx : 0));
+    for (int s = 0; s < 4; ++s) {
+      x[2 * s] = __ldcg(reinterpret_cast<const float2*>(qrow + 16 * s));
+      x[2 * s + 1] = __ldcg(reinterpret_cast<const float2*>(qrow + 16 * s + 8));
     }
 #pragma unroll
-    for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * NT;
-      if (idx < kGqa * kHeadDim) {
-        const int h = idx >> 6, d = idx & 63;
-        const int cc = d >> 3, e = d & 7;
-        S.q[((h * 2 + (e >> 2)) * 8 + cc) * 4 + (e & 3)] = qv[r] * 0.125f;
-      }
+    for (int s = 0; s < 4; ++s) {
+      const float sc = gq < kGqa ? 0.125f : 0.f;
+      split2(x[2 * s].x * sc, x[2 * s].y * sc, qa[s][0], qa[s][1]);
+      split2(x[2 * s + 1].x * sc, x[2 * s + 1].y * sc, qa[s][2], qa[s][3]);
     }
   }
-  sync();
 
-  float m[HPG], l[HPG], acc[HPG][2];
+  float m = -INFINITY, l = 0.f;  // running max and this thread's share of the sum (head gq)
+  float o[8][4];                 // O: dim tile d, rows gq (hi part) and gq + 8 (lo part)
 #pragma unroll
-  for (int hi = 0; hi < HPG; ++hi) {
-    m[hi] = -INFINITY;
-    l[hi] = 0.f;
-    acc[hi][0] = acc[hi][1] = 0.f;
-  }
+  for (int d = 0; d < 8; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
 
+  const int kw = warp * kWarpKeys;
+  // ldmatrix row addresses of this lane: matrix j = lane >> 3, row lane & 7
+  const int lj = lane >> 3, lr = lane & 7;
   for (int i = 0; i < ntiles; ++i) {
-    const int st = i & 1;
-    mbar_wait(&S.bar[st], parity(i), p.err);
+    if (i == ntiles - 1) cp_async_wait<0>();
+    else cp_async_wait<1>();
+    __syncthreads();
     const int k0 = kbeg + i * kTile;
     const int nk = min(kTile, kend - k0);
-    const int kw = 32 * kgrp;
-    const int nkw = max(0, min(32, nk - kw));
-    if (nkw > 0) {
-      const bool valid = lane < nkw;
-      float s[HPG];
+    if (kw < nk) {
+      const uint32_t st = (uint32_t)(i & 1) * kStageBytes;
+      // S = Q K^T for the warp's two 8-key n-tiles: ldmatrix of keys kw + 8t + lr, chunks
+      // 4h + lj (k-steps 2h and 2h + 1)
+      float sacc[2][4];
 #pragma unroll
-      for (int hi = 0; hi < HPG; ++hi) s[hi] = 0.f;
-      const uint16_t* krow = S.k[st] + (kw + lane) * kHeadDim;
+      for (int t = 0; t < 2; ++t) {
+        sacc[t][0] = sacc[t][1] = sacc[t][2] = sacc[t][3] = 0.f;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const int cc = (c + lane) & 7;
-        const uint4 kv = *reinterpret_cast<const uint4*>(krow + cc * 8);
-        const float k0f = bf16lo(kv.x), k1f = bf16hi(kv.x), k2f = bf16lo(kv.y), k3f = bf16hi(kv.y);
-        const float k4f = bf16lo(kv.z), k5f = bf16hi(kv.z), k6f = bf16lo(kv.w), k7f = bf16hi(kv.w);
-#pragma unroll
-        for (int hi = 0; hi < HPG; ++hi) {
-          if (hi < nh) {
-            const int h = h0 + hi;
-            const float4 qa = *reinterpret_cast<const float4*>(&S.q[((h * 2 + 0) * 8 + cc) * 4]);
-            const float4 qb = *reinterpret_cast<const float4*>(&S.q[((h * 2 + 1) * 8 + cc) * 4]);
-            float a = s[hi];
-            a = fmaf(qa.x, k0f, a);
-            a = fmaf(qa.y, k1f, a);
-            a = fmaf(qa.z, k2f, a);
-            a = fmaf(qa.w, k3f, a);
-            a = fmaf(qb.x, k4f, a);
-            a = fmaf(qb.y, k5f, a);
-            a = fmaf(qb.z, k6f, a);
-            a = fmaf(qb.w, k7f, a);
-            s[hi] = a;
-          }
+        for (int h = 0; h < 2; ++h) {
+          uint32_t b[4];
+          ldsm4(sk0 + st + swz(kw + 8 * t + lr, 4 * h + lj), b);
+          mma16816(sacc[t], qa[2 * h][0], qa[2 * h][1], qa[2 * h][2], qa[2 * h][3], b[0], b[1]);
+          mma16816(sacc[t], qa[2 * h + 1][0], qa[2 * h + 1][1], qa[2 * h + 1][2], qa[2 * h + 1][3], b[2], b[3]);
         }
       }
+      // scores of head gq for keys kw + 8t + 2qd + e (hi row + lo row), masked past nk
+      float sc[2][2];
+      float mx = -INFINITY;
 #pragma unroll
-      for (int hi = 0; hi < HPG; ++hi) {
-        if (hi < nh) {
-          const float sv = valid ? s[hi] : -INFINITY;
-          const float mn = fmaxf(m[hi], warp_max(sv));
-          const float alpha = expf(m[hi] - mn);
-          const float pr = valid ? expf(sv - mn) : 0.f;
-          l[hi] = l[hi] * alpha + warp_sum(pr);
-          acc[hi][0] *= alpha;
-          acc[hi][1] *= alpha;
-          m[hi] = mn;
-          S.p[kgrp][lane][h0 + hi] = pr;
-        }
-      }
-      __syncwarp();
-      const uint16_t* vt = S.v[st] + kw * kHeadDim + 2 * lane;
-#pragma unroll 4
-      for (int j = 0; j < nkw; ++j) {
-        const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vt + j * kHeadDim);
-        const float v0 = bf16lo(v2), v1 = bf16hi(v2);
-        float pv[HPG];
-        if constexpr (HPG == 4) {
-          const float4 pa = *reinterpret_cast<const float4*>(&S.p[kgrp][j][h0]);
-          pv[0] = pa.x; pv[1] = pa.y; pv[2] = pa.z; pv[3] = pa.w;
-        } else {
-          const float4 pa = *reinterpret_cast<const float4*>(&S.p[kgrp][j][0]);
-          const float4 pb = *reinterpret_cast<const float4*>(&S.p[kgrp][j][4]);
-          pv[0] = pa.x; pv[1] = pa.y; pv[2] = pa.z; pv[3] = pa.w; pv[4] = pb.x; pv[5] = pb.y; pv[6] = pb.z;
-        }
+      for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int hi = 0; hi < HPG; ++hi) {
-          acc[hi][0] = fmaf(pv[hi], v0, acc[hi][0]);
-          acc[hi][1] = fmaf(pv[hi], v1, acc[hi][1]);
+        for (int e = 0; e < 2; ++e) {
+          const bool valid = kw + 8 * t + 2 * qd + e < nk;
+          sc[t][e] = valid ? sacc[t][e] + sacc[t][2 + e] : -INFINITY;
+          mx = fmaxf(mx, sc[t][e]);
         }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m, mx);
+      const float alpha = expf(m - mn);
+      m = mn;
+      float pr[2][2];
+      float ps_ = 0.f;
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          pr[t][e] = sc[t][e] == -INFINITY ? 0.f : expf(sc[t][e] - mn);
+          ps_ += pr[t][e];
+        }
+      l = l * alpha + ps_;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) {
+        o[d][0] *= alpha;
+        o[d][1] *= alpha;
+        o[d][2] *= alpha;
+        o[d][3] *= alpha;
       }
-      __syncwarp();
+      // P as the A operand over the warp's 16 keys: k columns 2qd, 2qd + 1 = n-tile 0,
+      // 2qd + 8, 2qd + 9 = n-tile 1; row gq = p_hi, row gq + 8 = p_lo
+      uint32_t pa[4];
+      split2(pr[0][0], pr[0][1], pa[0], pa[1]);
+      split2(pr[1][0], pr[1][1], pa[2], pa[3]);
+      // O += P V: ldmatrix.trans of keys kw + 8 (lj & 1) + lr, chunks 2h + (lj >> 1)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        uint32_t b[4];
+        ldsm4_t(sv0 + st + swz(kw + 8 * (lj & 1) + lr, 2 * h + (lj >> 1)), b);
+        mma16816(o[2 * h], pa[0], pa[1], pa[2], pa[3], b[0], b[1]);
+        mma16816(o[2 * h + 1], pa[0], pa[1], pa[2], pa[3], b[2], b[3]);
+      }
     }
-    sync();  // stage st fully consumed
-    if (tid < 8 && i + 2 < ntiles) issue(i + 2);
+    __syncthreads();  // stage i & 1 fully consumed
+    if (i + 2 < ntiles) {
+      issue(i + 2, kend);
+      cp_async_commit();
+    }
   }
 
-  // Merge the 4 key groups. Their partials (acc[64], m, l per key group and head) take the
-  // place of K tile 0, whose last reader was the loop above: the CTA's shared memory then
-  // fits three CTAs per SM.
-  float (&cmb)[4][kGqa][kHeadDim + 2] = *reinterpret_cast<float (*)[4][kGqa][kHeadDim + 2]>(&S.k[0][0]);
-  static_assert(sizeof(float) * 4 * kGqa * (kHeadDim + 2) <= sizeof(S.k[0]), "key-group partials fit a K tile");
+  // Merge the 8 warps. Their partials (O[64], m, l per warp and head) take the place of
+  // K tile 0, whose last reader was the loop above.
+  float (&cmb)[kAttnWarps][kGqa][kHeadDim + 2] =
+      *reinterpret_cast<float (*)[kAttnWarps][kGqa][kHeadDim + 2]>(&S.k[0][0]);
+  static_assert(sizeof(float) * kAttnWarps * kGqa * (kHeadDim + 2) <= sizeof(S.k[0]), "warp partials fit a K tile");
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if (gq < kGqa) {
 #pragma unroll
-  for (int hi = 0; hi < HPG; ++hi) {
-    if (hi < nh) {
-      const int h = h0 + hi;
-      cmb[kgrp][h][2 * lane] = acc[hi][0];
-      cmb[kgrp][h][2 * lane + 1] = acc[hi][1];
-      if (lane == 0) {
-        cmb[kgrp][h][kHeadDim] = m[hi];
-        cmb[kgrp][h][kHeadDim + 1] = l[hi];
-      }
+    for (int d = 0; d < 8; ++d) {
+      cmb[warp][gq][8 * d + 2 * qd] = o[d][0] + o[d][2];
+      cmb[warp][gq][8 * d + 2 * qd + 1] = o[d][1] + o[d][3];
+    }
+    if (qd == 0) {
+      cmb[warp][gq][kHeadDim] = m;
+      cmb[warp][gq][kHeadDim + 1] = l;
     }
   }
-  sync();
+  __syncthreads();
   // this split's partial: (A[64], m, l) per head, in global scratch, in split 0's
   // shared memory (cluster: split 0 writes its own, the others over distributed shared
   // memory), or straight to the output when there is a single split
@@ -266,15 +333,15 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     *waited = true;
   }
   const uint32_t remote = push ? map_rank(&cm->recv[split][0], 0) : 0u;
-  for (int idx = tid; idx < kGqa * (kHeadDim + 2); idx += NT) {
+  for (int idx = tid; idx < kGqa * (kHeadDim + 2); idx += kAttnThreads) {
     const int h = idx / (kHeadDim + 2);
     const int d = idx - h * (kHeadDim + 2);
     float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, cmb[w][h][kHeadDim]);
+    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, cmb[w][h][kHeadDim]);
     float L = 0.f, A = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < kAttnWarps; ++w) {
       const float mw = cmb[w][h][kHeadDim];
       if (mw == -INFINITY) continue;
       const float sc = expf(mw - mx);
@@ -301,14 +368,14 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
 
   if (cm) {
     // split 0: its own partial is in place (barrier) and every other split's has arrived
-    sync();
+    __syncthreads();
     mbar_wait_cluster(&cm->bar, 0, p.err);
   } else {
     // Split merge by the last-arriving CTA of this (token, head): the barrier orders every
     // thread's partial stores before thread 0's acq_rel arrival.
-    sync();
+    __syncthreads();
     if (tid == 0) S.last = atomic_add_acq_rel(&p.counters[tok * kKvHeads + g], 1u) == (unsigned int)(nsplit - 1);
-    sync();
+    __syncthreads();
     if (!S.last) return false;
   }
   const float* base = p.part + (((long long)tok * kKvHeads + g) * p.max_splits) * kPartStride;
@@ -320,13 +387,13 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
   // area: 2 * 7 * nsplit + 7 floats), (2) per head the max and the split weights
   // exp(m_s - max), (3) the weighted sum of the split outputs, loads before stores.
   float* sm = &cmb[0][0][0];
-  for (int idx = tid; idx < kGqa * nsplit; idx += NT) {
+  for (int idx = tid; idx < kGqa * nsplit; idx += kAttnThreads) {
     const int h = idx / nsplit, s = idx - h * nsplit;
     const float mv = load(s, h * (kHeadDim + 2) + kHeadDim), lv = load(s, h * (kHeadDim + 2) + kHeadDim + 1);
     sm[idx] = mv;
     sm[kGqa * nsplit + idx] = lv;
   }
-  sync();
+  __syncthreads();
   if (tid < kGqa) {
     const int h = tid;
     float mx = -INFINITY;
@@ -339,9 +406,9 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     }
     sm[2 * kGqa * nsplit + h] = L;
   }
-  sync();
+  __syncthreads();
   {
-    constexpr int kRounds = (kGqa * kHeadDim + NT - 1) / NT;
+    constexpr int kRounds = (kGqa * kHeadDim + kAttnThreads - 1) / kAttnThreads;
     float A[kRounds];
 #pragma unroll
     for (int r = 0; r < kRounds; ++r) A[r] = 0.f;
@@ -349,7 +416,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     for (int s = 0; s < nsplit; ++s) {
 #pragma unroll
       for (int r = 0; r < kRounds; ++r) {
-        const int idx = tid + r * NT;
+        const int idx = tid + r * kAttnThreads;
         if (idx < kGqa * kHeadDim) {
           const int h = idx >> 6, d = idx & 63;
           A[r] = fmaf(sm[h * nsplit + s], load(s, h * (kHeadDim + 2) + d), A[r]);
@@ -358,7 +425,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     }
 #pragma unroll
     for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * NT;
+      const int idx = tid + r * kAttnThreads;
       if (idx < kGqa * kHeadDim) emit(p, tok, g * kGqa * kHeadDim + idx, A[r] / sm[2 * kGqa * nsplit + (idx >> 6)]);
     }
   }

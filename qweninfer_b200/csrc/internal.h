@@ -74,6 +74,10 @@ struct AttnParams {
   float* part;
   unsigned int* counters;
   int* err;
+  // 1: every query token is the only one of its cache row in this launch's forward and
+  // positions, rows and the cached keys below each position were written before it (a
+  // decode step): they are read before the programmatic-launch wait
+  int decode;
   // 1: the key splits of a (token, KV head) form one thread-block cluster of max_splits
   // CTAs (2..8) and are merged in split 0's shared memory; 0: merged through part/counters
   int cluster;

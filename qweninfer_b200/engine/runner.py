@@ -181,7 +181,7 @@ class DecodeRunner:
         if g is not None:
             g.replay()
         else:
-            self.ws.plan(B)
+            self.ws.plan(B, 1)  # one token per row: a decode step
             self._forward(self.dec, B, self.ws, 0, B)
             if self.cuda_graphs:
                 g = torch.cuda.CUDAGraph()
@@ -206,7 +206,7 @@ class DecodeRunner:
                 self.cache.reserve(row_start + b, int(q) + 1)
             self.cache.sync()
         self.dec.put(toks, pos, np.arange(row_start, row_start + B))
-        self.ws.plan(B)
+        self.ws.plan(B, 1)
         cap = 8 * (2 + 5 * self.model.cfg.num_hidden_layers)
         kinds = (C.c_int * cap)()
         us = (C.c_float * cap)()

@@ -278,13 +278,22 @@ class Block(nn.Module):
 # ------------------------------------------------------------- scratch space
 
 def _split_plan(max_tokens: int, max_len: int) -> tuple[int, int]:
-    """Key-split size and count for attention over `max_len` cache slots. Decode batches
-    (M <= 128) must fill 148 SMs: 128 keys per split while that gives at most 8 splits,
-    whose merge then runs inside one thread-block cluster (serving bench: decode step 1.19
-    -> 1.12 ms against 256-key splits), else 256 (measured best over 128/256/512/1024 with
-    the merge through global scratch: batch-128 decode at contexts 128..3000 3.80 -> 3.41
-    ms against 1024). Prefill-sized M: 1024."""
-    split = (128 if -(-max_len // 128) <= 8 else 256) if max_tokens <= 128 else 1024
+    """Key-split size and count for attention over `max_len` cache slots. A split costs a
+    merge (max-rescaled sums, in a thread-block cluster for 2-8 splits) and buys CTAs; with
+    the tensor-core tile loop (~0.2 us per 128 keys) the merge dominates short rows.
+    Measured on graph-replayed decode steps (ms, B = decode batch):
+    max_len <= 1024 — one split: B 32 / 128 at contexts ~300, max_len 512: 0.989 / 1.626
+    against 1.012 / 1.808 with 256-key splits (B 1: equal); max_len 4096 — 512 keys (8
+    splits) up to B 32: B 32 at contexts ~1000 1.142 (256: 1.168, 1024: 1.185), B 1 at
+    ~3000 0.954 (256: 1.075); 2048 keys beyond: B 64 at ~2000 1.608 (512: 1.792), B 128
+    2.519 (1024: 2.500, 256: 3.028). Prefill-sized M (the per-token kernel serves prompts
+    shorter than the block kernel's threshold): 1024."""
+    if max_tokens > 128:
+        split = 1024
+    elif max_len <= 1024:
+        split = -(-max_len // 128) * 128
+    else:
+        split = 512 if max_tokens <= 32 else 2048
     import os
     if os.environ.get("QI_ATTN_SPLIT"):  # tuning experiments: keys per split for every M
         split = max(128, int(os.environ["QI_ATTN_SPLIT"]) // 128 * 128)
@@ -364,7 +373,8 @@ class Workspace:
     def plan(self, M: int, query_run: int = 0) -> "Workspace":
         """Attention splits for M query tokens; `query_run`: the longest prompt among them
         (its tokens consecutive and in one cache row), 0 if unknown — it picks the prefill
-        attention kernel."""
+        attention kernel; 1 declares a decode step (one token per row, the rows' earlier
+        keys already cached), whose attention starts its copies early."""
         self.struct.split_keys, self.struct.max_splits = _split_plan(M, self.max_len)
         self.struct.query_run = query_run
         return self

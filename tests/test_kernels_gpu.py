@@ -182,13 +182,18 @@ def test_qkv_rope_append(M):
     (3, 512, [5, 127, 128]),
     (5, 1024, [0, 129, 255, 256, 1000]),
     (70, 700, None),
-    # the scaled serving cache (max_len 4096): <= 64 queries use 16 splits of 256 keys merged
-    # through global scratch, 128 queries 4 splits of 1024 keys merged in a cluster
+    # the scaled serving cache (max_len 4096): up to 32 queries 8 splits of 512 keys merged in
+    # a cluster, more queries 2 splits of 2048
     (2, 4096, [4095, 2047]),
     (64, 4096, None),
     (128, 4096, None),
+    # 16 splits of 512: merged by the last-arriving split through global scratch
+    (4, 8192, [8191, 5000, 100, 4096]),
 ])
 def test_attention_ragged(M, max_len, positions):
+    """The per-token kernel (decode batches and short prompts) against an fp64 reference.
+    Its tensor-core products carry q and p as hi/lo bf16 pairs (~16 mantissa bits), so the
+    bar is the reference's own fp32 component tolerance, 2e-5 (measured up to 1.3e-5)."""
     from qweninfer_b200.models.qwen2 import _AttnScratch
     rng = np.random.default_rng(M * 1000 + max_len)
     rows_total = 4
@@ -215,7 +220,7 @@ def test_attention_ragged(M, max_len, positions):
                 s = (kc[rows[t], g, :n] @ q[t, h * 64:(h + 1) * 64].astype(np.float64)) / 8.0
                 p = np.exp(s - s.max())
                 ref = (p / p.sum()) @ vc[rows[t], g, :n]
-                assert np.abs(got[t, h * 64:(h + 1) * 64] - ref).max() < 1e-5, (t, h)
+                assert np.abs(got[t, h * 64:(h + 1) * 64] - ref).max() < TOL_F32, (t, h)
 
 
 def _prefill_layout(lens, rows):

@@ -23,15 +23,17 @@ def test_split_plan_covers_every_key(M, max_len):
 
 
 @pytest.mark.parametrize("M", [1, 22, 128])
-@pytest.mark.parametrize("max_len", [96, 256, 512, 1024])
-def test_decode_splits_fit_one_cluster(M, max_len):
+@pytest.mark.parametrize("max_len", [96, 256, 512, 1000, 1024])
+def test_short_rows_are_one_split(M, max_len):
     split, n = _split_plan(M, max_len)
-    assert split == 128 and n <= 8
+    assert n == 1 and split >= max_len
 
 
-@pytest.mark.parametrize("M", [1, 64, 128])
-def test_long_context_decode_splits(M):
-    assert _split_plan(M, 4096) == (256, 16)
+@pytest.mark.parametrize("M,plan", [(1, (512, 8)), (32, (512, 8)), (33, (2048, 2)), (64, (2048, 2)),
+                                    (128, (2048, 2))])
+def test_long_context_decode_splits(M, plan):
+    """Up to batch 32 the splits of a 4096-slot row fill one thread-block cluster (8)."""
+    assert _split_plan(M, 4096) == plan
 
 
 def test_prefill_splits_are_coarse():
