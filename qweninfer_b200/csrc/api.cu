@@ -276,6 +276,16 @@ int l2_pf_distance() {
 // Split tiles of the per-stage projections, and attention's key splits, reduced inside
 // thread-block clusters (QI_TC_CLUSTER=0 turns it off for tuning experiments: partials
 // through global scratch and arrival counters everywhere).
+// QI_TC_KPU=1 keeps one 64-column k block per pipeline unit (comparisons)
+bool tc_units_of_two() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("QI_TC_KPU");
+    on = (e && atoi(e) == 1) ? 0 : 1;
+  }
+  return on != 0;
+}
+
 bool use_tc_clusters() {
   static int on = -1;
   if (on < 0) {
@@ -287,14 +297,14 @@ bool use_tc_clusters() {
 
 // How many clusters of C projection CTAs with this shared memory can be resident at once
 // (cached per configuration).
-int max_clusters(int epi, int NT, int stages, int C) {
+int max_clusters(int epi, int NT, int stages, int C, int kpu) {
   static std::map<long long, int> known;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  const long long key = ((((long long)dev * 8 + epi) * 256 + NT) * 64 + stages) * 16 + C;
+  const long long key = (((((long long)dev * 8 + epi) * 256 + NT) * 64 + stages) * 16 + C) * 4 + kpu;
   auto it = known.find(key);
   if (it != known.end()) return it->second;
-  const int n = tc_proj_max_clusters(epi, NT, stages, C);
+  const int n = tc_proj_max_clusters(epi, NT, stages, C, kpu);
   known[key] = n;
   return n;
 }
@@ -303,6 +313,11 @@ int max_clusters(int epi, int NT, int stages, int C) {
 // pipeline stages within the shared-memory budget, TMEM for two accumulators.
 int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* counters, int counters_len,
            int ctas, cudaStream_t s, bool pdl) {
+  // pipeline units of two 64-column k blocks where K allows: the MMA warp's fixed cost per
+  // unit (stage barrier wait ~110 ns after its UMMAs, commit, bookkeeping; measured) is
+  // then paid once per 128 columns
+  p.kpu = (p.KB % 2 == 0 && tc_units_of_two()) ? 2 : 1;
+  p.KB /= p.kpu;
   const long long units = (long long)p.n_mtiles * p.n_ntiles * p.KB;
   if ((long long)p.n_mtiles * p.n_ntiles > counters_len) return QI_ERR_ARG;
   int g = ctas > 0 ? ctas : sm_count();
@@ -312,7 +327,7 @@ int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* c
   if (g < 1) return QI_ERR_ARG;
   // Deep pipelines: a CTA streams at (bytes in flight) / (loaded DRAM latency, ~3 us), so
   // ~130 KB must be in flight per SM to reach the HBM rate.
-  const size_t stage = 16384 + (size_t)p.NT * 256;
+  const size_t stage = (size_t)p.kpu * (16384 + (size_t)p.NT * 256);
   int stages = (int)((size_t)tc_smem_budget_kb(p.NT) * 1024 / stage);
   stages = stages < 2 ? 2 : (stages > 12 ? 12 : stages);
   // Split tiles on thread-block clusters when every tile has the same number C (2..8) of
@@ -327,10 +342,10 @@ int run_tc(TcParams p, float* scratch, long long scratch_floats, unsigned int* c
     if (C > 8) C = 8;
     if (C > p.KB) C = p.KB;
     for (; C >= 2; --C) {
-      const size_t room = 227 * 1024 - tc_proj_smem(p.NT, 0, C);
+      const size_t room = 227 * 1024 - tc_proj_smem(p.NT, 0, C, p.kpu);
       int st = (int)(room / (stage + 16));
       if (st > stages) st = stages;
-      if (st >= 2 && tiles <= max_clusters(p.epi, p.NT, st, C)) {
+      if (st >= 2 && tiles <= max_clusters(p.epi, p.NT, st, C, p.kpu)) {
         p.cluster = C;
         stages = st;
         g = (int)(tiles * C);

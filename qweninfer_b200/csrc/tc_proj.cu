@@ -46,8 +46,12 @@ __global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams
   const int lane = threadIdx.x & 31;
   const int NT = p.NT;
   const int N = 2 * NT;
-  const uint32_t b_bytes = (uint32_t)NT * 256;
-  const uint32_t stage_bytes = kABytes + b_bytes;
+  const uint32_t b_bytes = (uint32_t)NT * 256;  // one 64-column block of the token tile
+  // a pipeline unit is kpu consecutive 64-column k blocks: kpu weight blocks, then kpu
+  // activation blocks (each run contiguous in HBM)
+  const int kpu = p.kpu;
+  const uint32_t a_unit = (uint32_t)kpu * kABytes, b_unit = (uint32_t)kpu * b_bytes;
+  const uint32_t stage_bytes = a_unit + b_unit;
   const int S = p.stages;
 
   uint8_t* stage_base = smem;
@@ -111,25 +115,25 @@ __global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams
       const int s = lane;
       uint8_t* st = stage_base + (size_t)s * stage_bytes;
       auto src_a = [&](int u) {
-        const int tile = u / p.KB, kb = u - tile * p.KB;
-        return p.w + ((long long)(tile / p.n_ntiles) * p.KB + kb) * (kABytes / 2);
+        const int tile = u / p.KB, ku = u - tile * p.KB;
+        return p.w + ((long long)(tile / p.n_ntiles) * p.KB + ku) * (a_unit / 2);
       };
       auto src_b = [&](int u) {
-        const int tile = u / p.KB, kb = u - tile * p.KB;
+        const int tile = u / p.KB, ku = u - tile * p.KB;
         const int nt = tile % p.n_ntiles + p.ntile0;
-        return p.act_in + ((long long)nt * p.KB + kb) * (b_bytes / 2);
+        return p.act_in + ((long long)nt * p.KB + ku) * (b_unit / 2);
       };
       if (s < nunits) {  // weights only: they do not depend on earlier kernels
         mbar_arrive_expect_tx(&full[s], stage_bytes);
-        bulk_g2s(st, src_a(u0 + s), kABytes, &full[s]);
+        bulk_g2s(st, src_a(u0 + s), a_unit, &full[s]);
       }
       grid_dep_wait();
-      if (s < nunits) bulk_g2s(st + kABytes, src_b(u0 + s), b_bytes, &full[s]);
+      if (s < nunits) bulk_g2s(st + a_unit, src_b(u0 + s), b_unit, &full[s]);
       for (int i = s + S; i < nunits; i += S) {
         mbar_wait(&empty[s], (uint32_t)(((i / S) & 1) ^ 1), p.err);
         mbar_arrive_expect_tx(&full[s], stage_bytes);
-        bulk_g2s(st, src_a(u0 + i), kABytes, &full[s]);
-        bulk_g2s(st + kABytes, src_b(u0 + i), b_bytes, &full[s]);
+        bulk_g2s(st, src_a(u0 + i), a_unit, &full[s]);
+        bulk_g2s(st + a_unit, src_b(u0 + i), b_unit, &full[s]);
       }
     } else {
       if (lane == 31 && p.pf_bytes > 0) {
@@ -163,11 +167,17 @@ __global__ void __launch_bounds__(kProjThreads, 1) tc_proj_kernel(const TcParams
           mbar_wait(&full[s], (uint32_t)((i / S) & 1), p.err);
           tc_fence_after();
           const uint32_t a_addr = smem_u32(stage_base + (size_t)s * stage_bytes);
-          const uint32_t b_addr = a_addr + kABytes;
+          // descriptor of a K-major operand at a_addr + off: its address field is (addr >> 4)
+          const uint64_t ad = kmajor_desc(a_addr), bd = kmajor_desc(a_addr + a_unit);
+          const uint64_t bd1 = bd + (b_bytes >> 4);  // the unit's second activation block
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(d_taddr, kmajor_desc(a_addr + kk * 256), kmajor_desc(b_addr + kk * 256), idesc,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+            umma_bf16(d_taddr, ad + (uint64_t)(kk * 16), bd + (uint64_t)(kk * 16), idesc, (j > 0 || kk > 0) ? 1u : 0u);
+          if (kpu == 2) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(d_taddr, ad + (uint64_t)((kABytes >> 4) + kk * 16), bd1 + (uint64_t)(kk * 16), idesc, 1u);
+          }
           umma_commit(&empty[s]);
         }
         umma_commit(&acc_full[b]);
@@ -229,8 +239,8 @@ __global__ void __launch_bounds__(256) act_tiles_kernel(const float* __restrict_
 
 }  // namespace
 
-size_t tc_proj_smem(int NT, int stages, int cluster) {
-  const size_t stage_bytes = kABytes + (size_t)NT * 256;
+size_t tc_proj_smem(int NT, int stages, int cluster, int kpu) {
+  const size_t stage_bytes = (size_t)kpu * (kABytes + (size_t)NT * 256);
   const size_t recv = cluster > 1 ? (size_t)(cluster - 1) * 128 * NT * 4 : 0;
   return (size_t)stages * stage_bytes + (size_t)stages * 16 + 48 + 16 + kEpiSmemBytes + recv;
 }
@@ -251,7 +261,7 @@ cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, boo
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas, 1, 1);
   cfg.blockDim = dim3(kProjThreads, 1, 1);
-  cfg.dynamicSmemBytes = tc_proj_smem(p.NT, p.stages, p.cluster);
+  cfg.dynamicSmemBytes = tc_proj_smem(p.NT, p.stages, p.cluster, p.kpu);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   int n = 0;
@@ -271,7 +281,7 @@ cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, boo
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-int tc_proj_max_clusters(int epi, int NT, int stages, int cluster) {
+int tc_proj_max_clusters(int epi, int NT, int stages, int cluster, int kpu) {
   void (*kern)(TcParams) = epi == kTcQkvRope    ? tc_proj_kernel<kTcQkvRope>
                            : epi == kTcQkvRopePaged ? tc_proj_kernel<kTcQkvRopePaged>
                            : epi == kTcResidual ? tc_proj_kernel<kTcResidual>
@@ -282,7 +292,7 @@ int tc_proj_max_clusters(int epi, int NT, int stages, int cluster) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cluster, 1, 1);
   cfg.blockDim = dim3(kProjThreads, 1, 1);
-  cfg.dynamicSmemBytes = tc_proj_smem(NT, stages, cluster);
+  cfg.dynamicSmemBytes = tc_proj_smem(NT, stages, cluster, kpu);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)cluster;

@@ -35,7 +35,8 @@ __host__ __device__ __forceinline__ long long act_offset(int t, int k, int part,
 struct TcParams {
   // A: weights (tiled), B: activation tiles
   const uint16_t* w;
-  int KB;          // 64-column blocks of K
+  int KB;          // pipeline units per output tile (K / 64 / kpu)
+  int kpu;         // 64-column k blocks per pipeline unit (1 or 2)
   int n_mtiles;    // weight rows / 128
   const uint16_t* act_in;
   int NT;          // token tile
@@ -89,10 +90,10 @@ struct TcParams {
   int* err;
 };
 
-size_t tc_proj_smem(int NT, int stages, int cluster);
+size_t tc_proj_smem(int NT, int stages, int cluster, int kpu);
 cudaError_t launch_tc_proj(const TcParams& p, int ctas, cudaStream_t stream, bool pdl);
 // clusters of `cluster` tc_proj CTAs that can be resident at once (0: none, or an error)
-int tc_proj_max_clusters(int epi, int NT, int stages, int cluster);
+int tc_proj_max_clusters(int epi, int NT, int stages, int cluster, int kpu);
 
 // x (M, K) fp32 -> activation tiles of (norm_w * x) (norm_w may be null) and, if ss is
 // non-null, per-token sums of squares of x in ss[0][t] (ss[1..6][t] = 0; K must be 896).
