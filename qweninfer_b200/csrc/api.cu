@@ -230,10 +230,10 @@ void token_tiles(int M, int nt[4]) {
   for (int i = 0; i < 4; ++i) nt[i] = env[i] ? env[i] : (i == 2 ? gu : t);
 }
 
-// Shared-memory budget of a tensor-core projection CTA for its pipeline stages, in KB, by
-// token tile: 144 for decode-sized tiles (<= 32; measured best over 96-192 at batches
-// 1-64), 192 for prefill-sized ones (1024-token prefill 4.80 -> 4.59 ms against 144).
-// QI_TC_SMEM_KB overrides both for tuning experiments.
+// Shared-memory budget of a tensor-core projection CTA for its pipeline stages, in KB:
+// 192 (with two-block pipeline units, against 144: decode step at batch 1 0.792 -> 0.775
+// ms, batches 22-64 0.3-0.4 % faster, 208 no better; 1024-token prefill 4.80 -> 4.59 ms).
+// QI_TC_SMEM_KB overrides it for tuning experiments.
 int tc_smem_budget_kb(int NT) {
   static int kb = -1;
   if (kb < 0) {
@@ -241,7 +241,8 @@ int tc_smem_budget_kb(int NT) {
     const int v = s ? atoi(s) : 0;
     kb = (v >= 48 && v <= 220) ? v : 0;
   }
-  return kb > 0 ? kb : (NT <= 32 ? 144 : 192);
+  (void)NT;
+  return kb > 0 ? kb : 192;
 }
 
 // Stream-K contributor caps of the forward's projections (qkv, o, gate/up, down, head):
