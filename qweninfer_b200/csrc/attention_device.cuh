@@ -69,6 +69,21 @@ __device__ __forceinline__ void emit(const AttnParams& p, int tok, int f, float 
 }
 
 // {bf16(a) in the low half, bf16(b) in the high half}
+__device__ __forceinline__ uint32_t bf16x2(float a, float b);
+
+// Output elements f and f + 1 (f even): one 8-byte fp32 store and one 4-byte store per
+// activation-tile half (the two features are neighbours in the tile layout).
+__device__ __forceinline__ void emit2(const AttnParams& p, int tok, int f, float v0, float v1) {
+  if (p.out) *reinterpret_cast<float2*>(p.out + (long long)tok * kHidden + f) = make_float2(v0, v1);
+  if (p.out_act) {
+    const uint32_t hi = bf16x2(v0, v1);
+    const uint32_t lo = bf16x2(v0 - __uint_as_float(hi << 16), v1 - __uint_as_float(hi & 0xffff0000u));
+    *reinterpret_cast<uint32_t*>(p.out_act + act_offset(tok, f, 0, kHidden, p.out_nt)) = hi;
+    *reinterpret_cast<uint32_t*>(p.out_act + act_offset(tok, f, 1, kHidden, p.out_nt)) = lo;
+  }
+}
+
+// {bf16(a) in the low half, bf16(b) in the high half}
 __device__ __forceinline__ uint32_t bf16x2(float a, float b) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
@@ -333,30 +348,62 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     *waited = true;
   }
   const uint32_t remote = push ? map_rank(&cm->recv[split][0], 0) : 0u;
-  for (int idx = tid; idx < kGqa * (kHeadDim + 2); idx += kAttnThreads) {
-    const int h = idx / (kHeadDim + 2);
-    const int d = idx - h * (kHeadDim + 2);
+  // (1) per head: the max over the warps, each warp's weight exp(m_w - max) and the
+  // weighted sum; (2) per pair of output dims: the weighted sum of the warps' O
+  float* wsc = &cmb[0][0][0] + kAttnWarps * kGqa * (kHeadDim + 2);  // [7][8] weights, [7] max, [7] sum
+  static_assert(sizeof(float) * (kAttnWarps * kGqa * (kHeadDim + 2) + kGqa * (kAttnWarps + 2)) <= sizeof(S.k[0]),
+                "warp weights fit after the partials");
+  if (tid < kGqa) {
+    const int h = tid;
     float mx = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, cmb[w][h][kHeadDim]);
-    float L = 0.f, A = 0.f;
+    float L = 0.f;
 #pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) {
       const float mw = cmb[w][h][kHeadDim];
-      if (mw == -INFINITY) continue;
-      const float sc = expf(mw - mx);
+      const float sc = mw == -INFINITY ? 0.f : expf(mw - mx);
       L = fmaf(sc, cmb[w][h][kHeadDim + 1], L);
-      if (d < kHeadDim) A = fmaf(sc, cmb[w][h][d], A);
+      wsc[h * kAttnWarps + w] = sc;
     }
-    const float val = d < kHeadDim ? A : (d == kHeadDim ? mx : L);
+    wsc[kGqa * kAttnWarps + h] = mx;
+    wsc[kGqa * (kAttnWarps + 1) + h] = L;
+    const int off = h * (kHeadDim + 2) + kHeadDim;  // m and l of the split's partial
+    if (nsplit > 1) {
+      if (!cm) {
+        part[off] = mx;
+        part[off + 1] = L;
+      } else if (split == 0) {
+        cm->recv[0][off] = mx;
+        cm->recv[0][off + 1] = L;
+      } else {
+        st_cluster_f32(remote + (uint32_t)off * 4u, mx);
+        st_cluster_f32(remote + (uint32_t)(off + 1) * 4u, L);
+      }
+    }
+  }
+  __syncthreads();
+  for (int e = tid; e < kGqa * kHeadDim / 2; e += kAttnThreads) {
+    const int h = e / (kHeadDim / 2), d = 2 * (e - h * (kHeadDim / 2));
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float sc = wsc[h * kAttnWarps + w];
+      const float2 v = *reinterpret_cast<const float2*>(&cmb[w][h][d]);
+      a0 = fmaf(sc, v.x, a0);
+      a1 = fmaf(sc, v.y, a1);
+    }
+    const int off = h * (kHeadDim + 2) + d;
     if (nsplit == 1) {
-      if (d < kHeadDim) emit(p, tok, (g * kGqa + h) * kHeadDim + d, A / L);
+      const float L = wsc[kGqa * (kAttnWarps + 1) + h];
+      emit2(p, tok, (g * kGqa + h) * kHeadDim + d, a0 / L, a1 / L);
     } else if (!cm) {
-      part[idx] = val;
+      *reinterpret_cast<float2*>(part + off) = make_float2(a0, a1);
     } else if (split == 0) {
-      cm->recv[0][idx] = val;
+      *reinterpret_cast<float2*>(&cm->recv[0][off]) = make_float2(a0, a1);
     } else {
-      st_cluster_f32(remote + (uint32_t)idx * 4u, val);
+      st_cluster_f32(remote + (uint32_t)off * 4u, a0);
+      st_cluster_f32(remote + (uint32_t)(off + 1) * 4u, a1);
     }
   }
   if (nsplit == 1) return true;
@@ -407,27 +454,20 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     sm[2 * kGqa * nsplit + h] = L;
   }
   __syncthreads();
-  {
-    constexpr int kRounds = (kGqa * kHeadDim + kAttnThreads - 1) / kAttnThreads;
-    float A[kRounds];
-#pragma unroll
-    for (int r = 0; r < kRounds; ++r) A[r] = 0.f;
+  for (int e = tid; e < kGqa * kHeadDim / 2; e += kAttnThreads) {
+    const int h = e / (kHeadDim / 2), d = 2 * (e - h * (kHeadDim / 2));
+    const int off = h * (kHeadDim + 2) + d;
+    float a0 = 0.f, a1 = 0.f;
 #pragma unroll 4
     for (int s = 0; s < nsplit; ++s) {
-#pragma unroll
-      for (int r = 0; r < kRounds; ++r) {
-        const int idx = tid + r * kAttnThreads;
-        if (idx < kGqa * kHeadDim) {
-          const int h = idx >> 6, d = idx & 63;
-          A[r] = fmaf(sm[h * nsplit + s], load(s, h * (kHeadDim + 2) + d), A[r]);
-        }
-      }
+      const float sc = sm[h * nsplit + s];
+      const float2 v = cm ? *reinterpret_cast<const float2*>(&cm->recv[s][off])
+                          : __ldcg(reinterpret_cast<const float2*>(base + (long long)s * kPartStride + off));
+      a0 = fmaf(sc, v.x, a0);
+      a1 = fmaf(sc, v.y, a1);
     }
-#pragma unroll
-    for (int r = 0; r < kRounds; ++r) {
-      const int idx = tid + r * kAttnThreads;
-      if (idx < kGqa * kHeadDim) emit(p, tok, g * kGqa * kHeadDim + idx, A[r] / sm[2 * kGqa * nsplit + (idx >> 6)]);
-    }
+    const float L = sm[2 * kGqa * nsplit + h];
+    emit2(p, tok, (g * kGqa + h) * kHeadDim + d, a0 / L, a1 / L);
   }
   if (!cm && tid == 0) p.counters[tok * kKvHeads + g] = 0u;
   return true;
