@@ -231,7 +231,8 @@ typedef struct {
   int query_run;            /* longest run of consecutive query tokens of one cache
                                row in the next forward (a prompt's length), or 0 if
                                unknown. Attention runs the prefill block kernel when
-                               it is >= 384 (0: when the forward has > 128 tokens).
+                               it is >= 1536 and more than half of the forward's
+                               tokens (0: when the forward has > 128 tokens).
                                1 declares a decode step: every token is the only one
                                of its row and the row's keys below its position are
                                in the cache before the call, so attention copies

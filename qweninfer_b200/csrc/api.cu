@@ -115,9 +115,11 @@ int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int3
   // query_run 1: a decode step (one query token per cache row, keys below it cached by
   // earlier forwards); the kernel then starts its copies before the previous launch ends
   a.decode = query_run == 1 ? 1 : 0;
-  // prompts of kBlockAttnMinRun tokens or more (or, length unknown, prefill-sized query
-  // counts): blocks of 16 consecutive tokens share K/V tiles on the tensor cores
-  if (use_block_attention() && (query_run > 0 ? query_run >= kBlockAttnMinRun : M > kBlockAttnMinTokens))
+  // a prompt of kBlockAttnMinRun tokens or more that is most of the forward (or, length
+  // unknown, prefill-sized query counts): blocks of 16 consecutive tokens share K/V tiles
+  // on the tensor cores
+  if (use_block_attention() &&
+      (query_run > 0 ? query_run >= kBlockAttnMinRun && 2LL * query_run > M : M > kBlockAttnMinTokens))
     return rc(launch_attention_block(a, s, pdl));
   // splits of a token merged inside a cluster when a launch has 2..8 of them
   a.cluster = (use_tc_clusters() && max_splits >= 2 && max_splits <= 8) ? 1 : 0;

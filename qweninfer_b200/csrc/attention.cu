@@ -29,12 +29,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
   ClusterMerge* cm = p.cluster ? reinterpret_cast<ClusterMerge*>(smem_raw + kMergeOffset) : nullptr;
-  // decode steps read positions and rows (written before the forward) without waiting for
-  // the previous launch; otherwise they may be its outputs
-  if (!p.decode) {
-    grid_dep_wait();
-    grid_dep_launch();
-  }
+  // Positions and rows are read before the programmatic-launch wait: they are inputs of the
+  // forward, written before its first launch (this kernel is never the first or second
+  // launch of a forward; standalone launches do not use programmatic launch). The wait is
+  // taken in attention_unit, by splits that have keys.
   const int tok = blockIdx.z;
   const int ps = p.pos[tok], row = p.rows[tok];
   if (cm && threadIdx.x == 0) {

@@ -19,12 +19,12 @@
 // through ldmatrix.trans (B of O = P V). Two stages; the copies of tile i + 2 are issued
 // after tile i.
 //
+// Positions and cache rows are read before the programmatic-launch wait, so key splits
+// without keys end at once instead of holding SM slots while the previous kernel runs.
 // Decode steps (AttnParams::decode: every query token is the only one of its cache row in
-// the forward) read the positions and cache rows and copy the first two tiles' cached keys
-// (positions < the query's own) before the programmatic-launch wait: those were written by
-// earlier forwards. Only the query and the key at the query's own position, which the
-// preceding QKV launch writes, are read after it. Key splits without keys end before the
-// wait, so they do not hold SM slots while the previous kernel runs.
+// the forward) also copy the first two tiles' cached keys (positions < the query's own)
+// before the wait: those were written by earlier forwards. Only the query and the key at
+// the query's own position, which the preceding QKV launch writes, are read after it.
 #pragma once
 
 #include "common.cuh"
@@ -129,10 +129,10 @@ __device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 12
 // (a single split, or the last split to arrive, which merges all of them).
 // cm: the cluster merge buffer (AttnParams::cluster), else null; *waited is set when the
 // unit waited on the cluster barrier (a split that pushes its partial to split 0 does so
-// before its first remote store). `ps` and `row` are the query's position and cache row.
-// With p.decode == 0 the caller has taken the programmatic-launch wait before reading
-// them; with p.decode == 1 it is taken here, after the first two tiles' cached keys are
-// requested, and units without keys return without it.
+// before its first remote store). `ps` and `row` are the query's position and cache row,
+// read by the caller before the programmatic-launch wait. The wait is taken here: before
+// the first copy (p.decode == 0) or after the first two tiles' cached keys are requested
+// (p.decode == 1); units without keys (and queries outside the cache) return without it.
 template <bool kPaged = false>
 __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S, int split, int g, int tok, int ps,
                                                int row, int tid, ClusterMerge* cm, bool* waited) {
@@ -210,6 +210,7 @@ __device__ __forceinline__ bool attention_unit(const AttnParams& p, AttnSmem& S,
     }
     cp_async_commit();
   } else {
+    dep_wait();
     issue(0, kend);
     cp_async_commit();
     if (ntiles > 1) issue(1, kend);

@@ -87,12 +87,14 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t stream, bool pdl)
 // Prefill form (attention_block.cu): one CTA per (16 consecutive query tokens, KV head);
 // uses q, kc, vc, pos, rows, M, max_len, cache_rows, out/out_act/out_nt, err.
 cudaError_t launch_attention_block(const AttnParams& p, cudaStream_t stream, bool pdl);
-// Forwards whose longest prompt has at least kBlockAttnMinRun tokens run
-// attention_block_kernel (shorter prompts: the per-token kernel's many CTAs measured
-// faster: 2.28 vs 2.60 ms to the first token of a 256-token prompt, 3.70 vs 3.38 at 512);
-// with the prompt length unknown, forwards of more than kBlockAttnMinTokens tokens do
-// (decode batches stay at or below it).
-constexpr int kBlockAttnMinRun = 384;
+// Forwards whose longest prompt has at least kBlockAttnMinRun tokens and is more than half
+// of the forward's tokens run attention_block_kernel; the per-token kernel (one key split
+// per query up to 4096 cache slots) measured faster below that: time to first token at a
+// 4096-slot cache 2.42 vs 2.92 ms at 384 tokens, 2.95 vs 3.42 at 512, 4.45 vs 4.53 at
+// 1024, batched prefills of 4 x 1024 and 2 x 2048 tokens 14.7 vs 15.3 and 17.6 vs 18.8 ms;
+// single prompts of 1536 and 2048 tokens 6.94 vs 6.71 and 9.30 vs 8.13 ms. With the prompt
+// length unknown, forwards of more than kBlockAttnMinTokens tokens run the block kernel.
+constexpr int kBlockAttnMinRun = 1536;
 constexpr int kBlockAttnMinTokens = 128;
 
 // slots (optional): the first n_slots argmax slots are zeroed. norm_w/NT/act/ss (optional,

@@ -286,10 +286,12 @@ def _split_plan(max_tokens: int, max_len: int) -> tuple[int, int]:
     against 1.012 / 1.808 with 256-key splits (B 1: equal); max_len 4096 — 512 keys (8
     splits) up to B 32: B 32 at contexts ~1000 1.142 (256: 1.168, 1024: 1.185), B 1 at
     ~3000 0.954 (256: 1.075); 2048 keys beyond: B 64 at ~2000 1.608 (512: 1.792), B 128
-    2.519 (1024: 2.500, 256: 3.028). Prefill-sized M (the per-token kernel serves prompts
-    shorter than the block kernel's threshold): 1024."""
+    2.519 (1024: 2.500, 256: 3.028). Prefill-sized M (the per-token kernel serves the
+    prompts below the block kernel's threshold): one split up to 4096 slots (a 512-token
+    prompt at a 4096-slot cache 3.84 -> 2.95 ms against 1024-key splits, which made 4-CTA
+    clusters of mostly empty splits)."""
     if max_tokens > 128:
-        split = 1024
+        split = min(-(-max_len // 128) * 128, 4096)
     elif max_len <= 1024:
         split = -(-max_len // 128) * 128
     else:

@@ -37,8 +37,9 @@ def test_long_context_decode_splits(M, plan):
 
 
 def test_prefill_splits_are_coarse():
-    assert _split_plan(512, 512) == (1024, 1)
-    assert _split_plan(129, 4096)[0] == 1024
+    assert _split_plan(512, 512) == (512, 1)
+    assert _split_plan(129, 4096) == (4096, 1)
+    assert _split_plan(4096, 8192) == (4096, 2)
 
 
 @pytest.mark.parametrize("rule", [token_tile, gate_up_tile])
