@@ -80,13 +80,15 @@ int qkv(const float* x, const float* ln_w, float eps, const uint16_t* w_qkv, con
 
 bool use_tc_clusters();
 
-// QI_BLOCK_ATTN=0 keeps the per-token attention kernel for prefill too (comparisons)
-bool use_block_attention() {
-  static const bool on = [] {
+// QI_BLOCK_ATTN=0 keeps the per-token attention kernel for prefill too, =2 runs the block
+// kernel for every forward of more than kBlockAttnMinTokens tokens (comparisons, profiles);
+// otherwise the kernel is chosen by the forward's longest prompt
+int block_attention_mode() {
+  static const int mode = [] {
     const char* v = getenv("QI_BLOCK_ATTN");
-    return !(v && v[0] == '0');
+    return v && v[0] == '0' ? 0 : (v && v[0] == '2' ? 2 : 1);
   }();
-  return on;
+  return mode;
 }
 
 int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int32_t* pos, const int32_t* rows,
@@ -118,8 +120,10 @@ int attention(const float* q, const uint16_t* kl, const uint16_t* vl, const int3
   // a prompt of kBlockAttnMinRun tokens or more that is most of the forward (or, length
   // unknown, prefill-sized query counts): blocks of 16 consecutive tokens share K/V tiles
   // on the tensor cores
-  if (use_block_attention() &&
-      (query_run > 0 ? query_run >= kBlockAttnMinRun && 2LL * query_run > M : M > kBlockAttnMinTokens))
+  const int bm = block_attention_mode();
+  if (bm == 2 ? M > kBlockAttnMinTokens
+              : bm == 1 && (query_run > 0 ? query_run >= kBlockAttnMinRun && 2LL * query_run > M
+                                          : M > kBlockAttnMinTokens))
     return rc(launch_attention_block(a, s, pdl));
   // splits of a token merged inside a cluster when a launch has 2..8 of them
   a.cluster = (use_tc_clusters() && max_splits >= 2 && max_splits <= 8) ? 1 : 0;
