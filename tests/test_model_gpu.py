@@ -244,6 +244,36 @@ def test_forward_writes_only_head_slots(gpu_model):
     assert bool((slots[1:] == sentinel).all())
 
 
+def test_decode_hint_changes_nothing(gpu_model):
+    """A forward declared a decode step (`query_run` 1: attention copies each row's cached
+    keys before the previous launch has finished, and only the key at the query's own
+    position after it) gives bit-identical logits to the same forward without the hint,
+    with rows spanning one to eight key splits of a 4096-slot cache."""
+    import ctypes as C
+    from qweninfer_b200 import _lib
+    B, max_len, V, L = 4, 4096, gpu_model.cfg.vocab_size, _lib.lib()
+    cache = KVCache(gpu_model.cfg, B, max_len, dtype=torch.bfloat16, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    cache.k.copy_(torch.randn(cache.k.shape, generator=g, device="cuda").to(torch.bfloat16))
+    cache.v.copy_(torch.randn(cache.v.shape, generator=g, device="cuda").to(torch.bfloat16))
+    ids = torch.tensor([11, 2024, 77, 150000], dtype=torch.int32, device="cuda")
+    pos = torch.tensor([0, 130, 1500, 4000], dtype=torch.int32, device="cuda")
+    rows = torch.tensor([2, 0, 3, 1], dtype=torch.int32, device="cuda")
+    out = []
+    for hint in (0, 1):
+        ws = gpu_model.workspace(B, max_len).plan(B, hint)
+        logits = torch.empty(B, V, dtype=torch.float32, device="cuda")
+        slots = torch.zeros(B, dtype=torch.int64, device="cuda")
+        _lib.check(L.qi_forward(C.byref(gpu_model.native()), C.byref(cache.native()), C.byref(ws.struct),
+                                ids.data_ptr(), pos.data_ptr(), rows.data_ptr(), B, 0, 1, B, logits.data_ptr(), 0,
+                                V, slots.data_ptr(), _lib.stream_ptr(gpu_model.device)), "qi_forward")
+        torch.cuda.synchronize()
+        ws.check()
+        out.append((logits.cpu(), slots.cpu()))
+    assert torch.equal(out[0][0], out[1][0])
+    assert torch.equal(out[0][1], out[1][1])
+
+
 def test_launch_times_match_the_forward(gpu_model):
     """qi_forward_launch_times runs the same launches as a decode step: embed, 24 x (qkv,
     attention, o, gate/up, down), head, each with a positive time; its greedy tokens equal
